@@ -1,0 +1,503 @@
+"""Benchmark of the FOLD draft-step hot path: side-cache append + rotated far read + merge.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl fold|reference]
+
+One step is one drafter layer's draft step: append the tokens accepted by the previous step
+(1..B, drawn from the seed) to the side cache, read the far memory with the query rotated to the
+shared far position (split-KV, fused rotation), and merge with the window read by LSE. With N
+ranks (torchrun) the side cache is partitioned by contiguous position chunks; each rank reads its
+chunk, combines its splits, the per-rank partials are all-gathered over NCCL and merged.
+
+Workloads (synthetic, seeded; random-init drafter shapes):
+  2 (default): Llama-3.1-8B drafter, 32 q / 8 kv heads, hd 128, B 10, context 131072, W 2048,
+     alpha 2, K/V N(0,1) with 4 outlier channels per head x8, theta 5e5.
+  3: Qwen3-8B drafter, 32/8, hd 128, B 8, context 32768, W 2048, theta 1e6.
+  4: 16/4 heads, hd 256, B 16, context 262144, W 4096.
+  5: 16/8 heads, hd 256, B 8, context 262144, W 4096.
+The window read's (o, lse) are synthetic inputs resident in HBM (that read is not part of this
+path). The side cache (0.5-2 GB) is far larger than L2 (126 MB), so no flush is needed between
+steps.
+
+Prints one JSON line (rank 0). value = microseconds per draft step (max over ranks, CUDA events).
+--impl reference times the CPU oracle port of the same step on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    2: dict(name="llama3.1-8b-drafter-128k", hq=32, hkv=8, hd=128, B=10, ctx=131072, W=2048, theta=5e5, outliers=4),
+    3: dict(name="qwen3-8b-drafter-32k", hq=32, hkv=8, hd=128, B=8, ctx=32768, W=2048, theta=1e6, outliers=0),
+    4: dict(name="hd256-16q4kv-262k", hq=16, hkv=4, hd=256, B=16, ctx=262144, W=4096, theta=1e6, outliers=0),
+    5: dict(name="hd256-16q8kv-262k", hq=16, hkv=8, hd=256, B=8, ctx=262144, W=4096, theta=1e6, outliers=0),
+}
+ALPHA = 2.0
+METRIC = "us/draft-step (FOLD far-read + merge)"
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="fold", choices=["fold", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--splits", type=int, default=0, help="far-read splits per KV head (0: one CTA per SM)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------ clocks sampler
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), active=parts[4], hw=parts[5],
+                                 hw_thermal=parts[6], sw_thermal=parts[7], power_cap=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        loaded = [r for r in rows if r["sm"] > 0.5 * r["max"]] or rows
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
+                              ("sw_thermal", "sw_thermal_slowdown"), ("power_cap", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------ workload
+def plan_steps(cfg, total_steps, seed):
+    """Accepted tokens per step (1..B uniform from the seed) and the committed context H of each
+    step; the first step sees a context of exactly cfg['ctx'] positions (H0 = ctx - B)."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed + 1)
+    acc = rng.integers(1, cfg["B"] + 1, size=total_steps)
+    H = np.empty(total_steps, dtype=np.int64)
+    H[0] = cfg["ctx"] - cfg["B"]
+    for i in range(1, total_steps):
+        H[i] = H[i - 1] + acc[i - 1]
+    return acc, H
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(cfg_id):
+    """DRAM bytes per far-read launch from the committed ncu summary of this workload, if any."""
+    f = ROOT / "profiles" / f"far_read_config{cfg_id}.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------------------------ CPU legs
+def cpu_step_oracle(cfg, H, q, k, v, o_l, lse_l, inv_freq):
+    """The oracle's far query + far read + merge of one step (float64 numpy)."""
+    from oracle import fold_oracle as fo
+
+    W, B = cfg["W"], cfg["B"]
+    qf = fo.bf16_round(fo.far_query(q, H, inv_freq, W + B))
+    lim = fo.far_row_limits(H, W, B, B)
+    L = int(lim.max())
+    o_f, lse_f = fo.far_read(qf, k[:L], v[:L], lim, cfg["hd"] ** -0.5 * ALPHA)
+    return fo.merge(o_l, lse_l, o_f, lse_f, H, W, B, ALPHA)
+
+
+def cpu_inputs(cfg, seed, max_keys):
+    import numpy as np
+
+    rng = np.random.default_rng(seed + 7)
+    L = max_keys
+    # a 4096-row block of N(0,1) keys/values tiled to the context: the oracle's cost does not
+    # depend on the values, and generating 10^8 normals would dominate the sample
+    reps = -(-L // 4096)
+    k = np.tile(rng.standard_normal((4096, cfg["hkv"], cfg["hd"])), (reps, 1, 1))[:L]
+    v = np.tile(rng.standard_normal((4096, cfg["hkv"], cfg["hd"])), (reps, 1, 1))[:L]
+    q = rng.standard_normal((cfg["B"], cfg["hq"], cfg["hd"])).astype(np.float64)
+    o_l = rng.standard_normal((cfg["B"], cfg["hq"], cfg["hd"]))
+    lse_l = rng.standard_normal((cfg["hq"], cfg["B"])) + 5.0
+    return q, k, v, o_l, lse_l
+
+
+def cpu_baseline(cfg, seed, budget_s=15.0, max_steps=50):
+    """Times the oracle port on the host cores: whole steps of the workload until ~budget_s."""
+    from oracle import fold_oracle as fo
+
+    acc, H = plan_steps(cfg, max_steps, seed)
+    q, k, v, o_l, lse_l = cpu_inputs(cfg, seed, int(H.max()))
+    f = fo.inv_freq(cfg["theta"], cfg["hd"])
+    cpu_step_oracle(cfg, int(H[0]), q, k, v, o_l, lse_l, f)  # warm-up
+    times = []
+    t_all = time.perf_counter()
+    for i in range(max_steps):
+        t0 = time.perf_counter()
+        cpu_step_oracle(cfg, int(H[i]), q, k, v, o_l, lse_l, f)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    us = 1e6 * statistics.mean(times)
+    return dict(value=us, unit="us/draft-step", cores=os.cpu_count() or 1, kind="port",
+                sample=f"{len(times)} whole draft steps of the {cfg['name']} workload (float64 numpy oracle: "
+                       f"far query + far read + merge, BLAS threads = {os.cpu_count()})")
+
+
+# ------------------------------------------------------------------------------ GPU arm
+def run_gpu(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from fold_b200 import kernels
+    from fold_b200.rope import default_inv_freq, rope_table
+    from fold_b200.shard import ShardPlan, unpack_partials
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = CONFIGS[args.config]
+    hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
+    total = args.warmup + args.steps
+    acc, H = plan_steps(cfg, total, args.seed)
+    length = int(H[-1] + acc[-1]) + B  # every position any step appends or reads
+    plan = ShardPlan.even(length, world, rank)
+    pos_lo, held = plan.pos_lo, plan.held
+    pages = -(-max(held, 1) // 256) + 1
+
+    # ---- side cache: the committed context before the first step, N(0,1) (+ outlier channels)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed * 1000 + rank)
+    side = torch.empty((pages, hkv, 256, 2 * hd), device=dev, dtype=torch.bfloat16)
+    side.normal_(generator=gen)
+    if cfg["outliers"]:
+        ch = torch.randperm(hd, generator=torch.Generator().manual_seed(args.seed))[: cfg["outliers"]]
+        cols = torch.cat((ch, ch + hd)).to(dev)
+        side[..., cols] *= 8.0
+    # accepted tokens of every step (K and V before RoPE), appended at their positions
+    max_acc = int(acc.max())
+    new_k = torch.randn((total, max_acc, hkv, hd), device=dev, dtype=torch.bfloat16, generator=gen)
+    new_v = torch.randn((total, max_acc, hkv, hd), device=dev, dtype=torch.bfloat16, generator=gen)
+    new_pos = torch.zeros((total, max_acc), device=dev, dtype=torch.int64)
+    for i in range(total):
+        new_pos[i, : acc[i]] = torch.arange(int(H[i]), int(H[i]) + int(acc[i]))
+    q_all = torch.randn((total, B, hq, hd), device=dev, dtype=torch.bfloat16, generator=gen)
+    seq_all = torch.from_numpy((H + B).astype(np.int32)).to(dev)
+    qsl = torch.tensor([0, B], dtype=torch.int32, device=dev)
+    o_l = torch.randn((B, hq, hd), device=dev, dtype=torch.bfloat16, generator=gen)
+    lse_l = (torch.randn((hq, B), device=dev, generator=gen) + 5.0).float()
+    out = torch.empty((B, hq, hd), device=dev, dtype=torch.bfloat16)
+    inv = default_inv_freq(cfg["theta"], hd, dev)
+    table = rope_table(inv, length + W + B + 1, dev)
+    splits = args.splits or kernels.default_splits(hkv)
+    o_part = torch.empty((splits, B, hq, hd), device=dev, dtype=torch.float32)
+    lse_part = torch.empty((splits, hq, B), device=dev, dtype=torch.float32)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    per = B * hq * hd + hq * B
+    send = torch.empty(per, device=dev, dtype=torch.float32)
+    recv = torch.empty(world * per, device=dev, dtype=torch.float32)
+    o_mine, lse_mine = send[: B * hq * hd].view(B, hq, hd), send[B * hq * hd:].view(hq, B)
+    scale = hd ** -0.5 * ALPHA
+    stream = torch.cuda.current_stream(dev)
+    ev_far = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def step(i, timed_idx=None):
+        a = int(acc[i - 1]) if i > 0 else 0
+        if a:  # tokens accepted by the previous step become committed context
+            kernels.append(new_k[i - 1, :a], new_v[i - 1, :a], new_pos[i - 1, :a], new_pos[i - 1, :a], side,
+                           pos_lo=pos_lo, skip_foreign=world > 1, err=err)
+        seq = seq_all[i: i + 1]
+        if timed_idx is not None:
+            ev_far[timed_idx][0].record(stream)
+        kernels.far_read(q_all[i], qsl, seq, side, o_part, lse_part, window=W, block=B, far_distance=W + B,
+                         softmax_scale=scale, table=table, pos_lo=pos_lo, capacity=length, err=err)
+        if timed_idx is not None:
+            ev_far[timed_idx][1].record(stream)
+        if world > 1:
+            kernels.combine(o_part, lse_part, o_mine, lse_mine)
+            dist.all_gather_into_tensor(recv, send)
+            o_all, lse_all = unpack_partials(recv, world, B, hq, hd)
+            kernels.merge(o_l, lse_l, o_all, lse_all, out, qsl, seq, window=W, block=B, alpha=ALPHA)
+        else:
+            kernels.merge(o_l, lse_l, o_part, lse_part, out, qsl, seq, window=W, block=B, alpha=ALPHA)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for j in range(args.steps):
+            step(args.warmup + j, j)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    far_ms = sum(a.elapsed_time(b) for a, b in ev_far) / args.steps
+    if int(err.item()):
+        raise RuntimeError(f"device error word {int(err.item())}")
+    t = torch.tensor([ms, far_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, far_ms = float(t[0]), float(t[1])
+    us_step = 1000.0 * ms / args.steps
+
+    # algorithmic bytes of one far-read launch on this rank: its K/V rows + q + partials
+    far_keys = [min(max(int(H[args.warmup + j]) - W, 0), pos_lo + held) - pos_lo for j in range(args.steps)]
+    kv_bytes = statistics.mean(max(f, 0) for f in far_keys) * hkv * 2 * hd * 2
+    part_bytes = splits * (B * hq * hd + hq * B) * 4
+    alg = kv_bytes + B * hq * hd * 2 + part_bytes
+    hbm_peak, peak_kind = peaks()
+    achieved = alg / (far_ms * 1e-3) / 1e9
+    traffic = profile_traffic(args.config) if world == 1 else None
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(us_step, 3),
+            "unit": "us/draft-step",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 6),
+            "higher_is_better": False,
+            "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) K/V/Q, random-init drafter shapes)",
+            "config": {"workload": cfg["name"], "context": cfg["ctx"], "window": W, "block": B, "heads_q": hq,
+                       "heads_kv": hkv, "head_dim": hd, "alpha": ALPHA, "splits": splits,
+                       "parallelism": f"seq-shard{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (side cache %.0f MB per GPU)" % (side.numel() * 2 / 1e6)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                         "kernel": "far_read_kernel", "kernel_us": round(far_ms * 1000, 3),
+                         "algorithmic_bytes": int(alg), "traffic": traffic},
+            "gpu_launches": args.steps * (3 if world == 1 else 4),
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+        }
+        if not args.no_cpu and world == 1:
+            line["cpu_baseline"] = cpu_baseline(cfg, args.seed)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local):
+    """The same steps through the public workspace API with pinned host inputs: per step the
+    query, the accepted K/V and their positions are copied host->device inside the timed region,
+    and the merged output is read back device->host."""
+    import torch
+    import torch.distributed as dist
+
+    from fold_b200.attention import FoldWorkspace
+    from fold_b200.shard import ShardedFarMemory, ShardPlan
+
+    hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
+    total = args.warmup + args.steps
+    dummy = torch.zeros((1, hkv, 16, 2 * hd), device=dev, dtype=torch.bfloat16)
+    plan = ShardPlan.even(length, world, rank)
+    ws = FoldWorkspace(dummy, W, B, length, inv_freq=torch.ones(hd // 2, device=dev), far_distance=W + B,
+                       alpha=ALPHA, num_heads=hq, splits=splits, pos_lo=plan.pos_lo,
+                       shard_len=plan.held if world > 1 else None)
+    ws.side = side  # the same resident side cache as the kernel leg
+    ws._table = table
+    sharded = ShardedFarMemory(plan, ws) if world > 1 else None
+    gen = torch.Generator().manual_seed(args.seed + 99)
+    max_acc = int(acc.max())
+    h_q = torch.randn((total, B, hq, hd), generator=gen).to(torch.bfloat16).pin_memory()
+    h_k = torch.randn((total, max_acc, hkv, hd), generator=gen).to(torch.bfloat16).pin_memory()
+    h_v = torch.randn((total, max_acc, hkv, hd), generator=gen).to(torch.bfloat16).pin_memory()
+    h_pos = torch.zeros((total, max_acc), dtype=torch.int64)
+    for i in range(total):
+        h_pos[i, : acc[i]] = torch.arange(int(H[i]), int(H[i]) + int(acc[i]))
+    h_pos = h_pos.pin_memory()
+    h_seq = torch.from_numpy((H + B).astype("int32")).reshape(total, 1).pin_memory()
+    h_out = torch.empty((B, hq, hd), dtype=torch.bfloat16).pin_memory()
+    d_q = torch.empty((B, hq, hd), device=dev, dtype=torch.bfloat16)
+    d_k = torch.empty((max_acc, hkv, hd), device=dev, dtype=torch.bfloat16)
+    d_v = torch.empty_like(d_k)
+    d_pos = torch.empty(max_acc, device=dev, dtype=torch.int64)
+    d_seq = torch.empty(1, device=dev, dtype=torch.int32)
+    qsl = torch.tensor([0, B], dtype=torch.int32, device=dev)
+    o_l = torch.randn((B, hq, hd), device=dev, dtype=torch.bfloat16)
+    lse_l = torch.randn((hq, B), device=dev) + 5.0
+    out = torch.empty((B, hq, hd), device=dev, dtype=torch.bfloat16)
+    h2d = d2h = 0
+    from fold_b200 import kernels
+
+    def step(i):
+        nonlocal h2d, d2h
+        a = int(acc[i - 1]) if i > 0 else 0
+        d_q.copy_(h_q[i], non_blocking=True)
+        d_seq.copy_(h_seq[i], non_blocking=True)
+        h2d_i = d_q.numel() * 2 + 4
+        if a:
+            d_k[:a].copy_(h_k[i - 1, :a], non_blocking=True)
+            d_v[:a].copy_(h_v[i - 1, :a], non_blocking=True)
+            d_pos[:a].copy_(h_pos[i - 1, :a], non_blocking=True)
+            h2d_i += 2 * a * hkv * hd * 2 + a * 8
+            ws.append(d_k[:a], d_v[:a], d_pos[:a], d_pos[:a])
+        if sharded is not None:
+            o_all, lse_all = sharded.step(d_q, qsl, d_seq, hd ** -0.5)
+            sharded.merge(o_l, lse_l, o_all, lse_all, out, qsl, d_seq)
+        else:
+            o_part, lse_part = ws.read_far(d_q, qsl, d_seq, hd ** -0.5)
+            kernels.merge(o_l, lse_l, o_part, lse_part, out, qsl, d_seq, window=W, block=B, alpha=ALPHA)
+        h_out.copy_(out, non_blocking=True)
+        return h2d_i, out.numel() * 2
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for j in range(args.steps):
+        a, b = step(args.warmup + j)
+        h2d += a
+        d2h += b
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return {"value": round(1000.0 * float(ms) / args.steps, 3), "unit": "us/draft-step",
+            "h2d_bytes_per_step": int(h2d / args.steps), "d2h_bytes_per_step": int(d2h / args.steps),
+            "api": "FoldWorkspace.append/read_far + kernels.merge (fold_b200 C-ABI), pinned host buffers"}
+
+
+# ------------------------------------------------------------------------------ reference arm
+def run_reference(args):
+    """The CPU implementation of the path (the oracle port; the reference's own GPU path needs
+    vLLM 0.28 and FlashAttention, and its CPU code is fold/reference.py, restated by the oracle),
+    on all host threads, on this arm's workload and metric."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    import numpy as np
+
+    from oracle import fold_oracle as fo
+
+    steps = max(1, min(args.steps, 10))
+    warm = max(0, min(args.warmup, 1))
+    acc, H = plan_steps(cfg, steps + warm, args.seed)
+    q, k, v, o_l, lse_l = cpu_inputs(cfg, args.seed, int(H.max()))
+    f = fo.inv_freq(cfg["theta"], cfg["hd"])
+    for i in range(warm):
+        cpu_step_oracle(cfg, int(H[i]), q, k, v, o_l, lse_l, f)
+    times = []
+    for i in range(warm, warm + steps):
+        t0 = time.perf_counter()
+        cpu_step_oracle(cfg, int(H[i]), q, k, v, o_l, lse_l, f)
+        times.append(time.perf_counter() - t0)
+    us = 1e6 * float(np.mean(times))
+    cores = os.cpu_count() or 1
+    sample = (f"{steps} whole draft steps of the {cfg['name']} workload: float64 numpy port of "
+              f"fold/reference.py's far read + merge (BLAS on {cores} threads)")
+    line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/draft-step",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": warm,
+            "ms_per_step": round(us / 1000, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": cfg["name"], "context": cfg["ctx"], "window": cfg["W"], "block": cfg["B"],
+                       "heads_q": cfg["hq"], "heads_kv": cfg["hkv"], "head_dim": cfg["hd"], "alpha": ALPHA},
+            "cpu_baseline": {"value": round(us, 1), "unit": "us/draft-step", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(us, 1), "unit": "us/draft-step", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

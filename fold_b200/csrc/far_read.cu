@@ -1,0 +1,575 @@
+// Far-memory read of FOLD (fold/attention.py:162-170 of the reference): far-query rotation fused
+// with a split-KV attention pass over the side cache, one CTA per (split, KV head).
+//
+// Per CTA: one producer warp streams tiles of TK keys of this head's K|V rows from the side cache
+// into a ring of shared-memory stages with TMA (128-byte swizzle, completion on mbarriers). Eight
+// consumer warps compute, per tile,
+//   S^T = K . Qf^T     (keys on the MMA M dimension, the n*G query rows on N: no row padding)
+//   P^T = exp2(S^T * scale * log2e - m)      (online softmax with a lazily raised row maximum)
+//   O^T += V^T . P^T
+// on bf16 mma.sync tiles, and finally write the split's normalised partial (o, lse).
+//
+// The running row maximum m only moves when a new logit exceeds it by more than 2^kRaise, which
+// is decided for the whole CTA by one OR-barrier per tile. So the common tile needs no cross-warp
+// max exchange and no rescaling; P stays below 2^kRaise (exact in fp32, fine in bf16).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace fold {
+
+constexpr float kRaise = 8.0f;
+
+struct FarParams {
+  const __nv_bfloat16* q;
+  int64_t q_st, q_sh;
+  const int* qsl;
+  const int* seq;
+  const float* table;
+  int table_rows, rot_dim;
+  int64_t pos_lo, capacity, local_cap;
+  int* far_len;
+  __nv_bfloat16* qf;
+  int64_t qf_st, qf_sh;
+  float* o_part;
+  float* lse_part;
+  int splits, n, hq, hkv, group;
+  int window, block, far_distance;
+  float scale_log2;
+  int* err;
+};
+
+constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100
+
+template <int HD_, int NT_, int TK_, int HG_>
+struct FarCfg {
+  static constexpr int HD = HD_, NT = NT_, TK = TK_, HG = HG_;
+  static constexpr int ROWS = 8 * NT;
+  static constexpr int NW = 8;  // warps; thread 0 also issues the TMA copies
+  static constexpr int NTHREADS = NW * 32;
+  static constexpr int KBOX = HD / 64;  // 64-column boxes per K (and per V) row block
+  static constexpr int BOX_BYTES = TK * 128;
+  static constexpr int STAGE_BYTES = 2 * KBOX * BOX_BYTES;
+  static constexpr int MT = TK / 16;  // key m-tiles per tile (one per QK warp column)
+  static constexpr int NG = NW / MT;  // QK warps sharing one m-tile split the n-tiles
+  static constexpr int QNT = (NT + NG - 1) / NG;
+  static constexpr int KG = NW / HG;  // PV: HG hd groups x KG key groups
+  static constexpr int PV_MT = HD / 16 / HG;
+  static constexpr int PV_KS = TK / 16 / KG;
+  static constexpr int QSTRIDE = HD + 8;                        // elements; 16-byte units odd
+  static constexpr int PSTRIDE = 8 * ((NT & 1) ? NT : NT + 1);  // elements; 16-byte units odd
+  static constexpr bool Q_REGS = QNT * (HD / 16) * 2 <= 80;
+  static constexpr int Q_BYTES = ROWS * QSTRIDE * 2;
+  static constexpr int P_BYTES = 2 * TK * PSTRIDE * 2;
+  static constexpr int RED_BYTES = MT * ROWS * 4;
+  static constexpr int ROW_BYTES = 2 * 64 * 4;
+  static constexpr int FIXED = Q_BYTES + P_BYTES + RED_BYTES + ROW_BYTES + 8 * 8 + 1024;
+  static constexpr int NSTAGE_FIT = (kSmemLimit - FIXED) / STAGE_BYTES;
+  static constexpr int NSTAGE = NSTAGE_FIT > 4 ? 4 : NSTAGE_FIT;
+  static constexpr int OFF_Q = NSTAGE * STAGE_BYTES;
+  static constexpr int OFF_P = OFF_Q + Q_BYTES;
+  static constexpr int OFF_RED = OFF_P + P_BYTES;
+  static constexpr int OFF_ROW = OFF_RED + RED_BYTES;
+  static constexpr int OFF_BAR = OFF_ROW + ROW_BYTES;
+  static constexpr int SMEM = OFF_BAR + 8 * 8 + 1024;
+  static_assert(NSTAGE >= 2, "shared memory too small for two stages");
+  static_assert(SMEM <= kSmemLimit, "shared memory budget");
+  static_assert(MT * NG == NW && HG * KG == NW, "warp split");
+  static_assert(PV_MT >= 1 && PV_KS >= 1, "warp split");
+  static_assert(ROWS * HD * 4 <= NSTAGE * STAGE_BYTES, "epilogue staging");
+  static_assert(TK <= 256 && 256 % TK == 0, "tiles stay inside one 256-entry page");
+};
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// Issues the TMA copies of tile `tile` (index in this cache) of head h into stage `st`.
+template <class C>
+__device__ __forceinline__ void issue_tile(unsigned char* smem, uint64_t* full, const CUtensorMap* map, int st,
+                                           int tile, int hkv, int h, uint64_t pol) {
+  mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+  const int64_t lp = static_cast<int64_t>(tile) * C::TK;
+  const int page = static_cast<int>(lp >> 8), off = static_cast<int>(lp & 255);
+  const int c2 = page * hkv + h;
+  unsigned char* dst = smem + st * C::STAGE_BYTES;
+#pragma unroll
+  for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
+}
+
+template <class C>
+__global__ void __launch_bounds__(C::NTHREADS, 1)
+    far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
+  constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
+  constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_Q);
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  float* row_m = reinterpret_cast<float*>(smem + C::OFF_ROW);
+  float* row_inv = row_m + 64;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x, h = blockIdx.y;
+
+  // Step geometry, from the device-side lengths (fold/kernels.py:24-30).
+  const int qlen = p.qsl[1] - p.qsl[0];
+  const int hist = max(p.seq[0] - qlen, 0);
+  const int far_len = max(hist - p.window - p.block + qlen, 0);
+  const int lim_base = hist - p.window - p.block + 1;  // row r reads positions [0, lim_base + r)
+  const int64_t end = min64(max(lim_base + p.n - 1, 0), p.pos_lo + p.local_cap);
+  const int64_t len = max64(end - p.pos_lo, 0);
+  const int tiles = static_cast<int>((len + TK - 1) / TK);
+  const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / p.splits);
+  const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / p.splits) - t_begin;
+
+  uint64_t pol = 0;
+  if (tid == 0) {
+    if (split == 0 && h == 0) {
+      if (p.far_len) *p.far_len = far_len;
+      if (far_len > p.capacity) set_error(p.err, FOLD_DEVERR_CAPACITY);
+    }
+#pragma unroll
+    for (int i = 0; i < NSTAGE; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    // Fill the ring right away, so the first copies overlap the query rotation below.
+    pol = l2_evict_first_policy();
+    prefetch_tensormap(&map);
+    for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue_tile<C>(smem, full, &map, i, t_begin + i, p.hkv, h, pol);
+  }
+
+  const int G = p.group;
+  const int nrows = p.n * G;
+
+  // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table.
+  {
+    const int delta = p.far_distance - hist;
+    int ad = delta < 0 ? -delta : delta;
+    const float sgn = delta < 0 ? -1.f : 1.f;
+    if (p.table && ad >= p.table_rows) {
+      if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
+      ad = p.table_rows - 1;
+    }
+    const int RH = p.rot_dim >> 1;
+    const float* trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
+    for (int e = tid; e < ROWS * HD; e += NTH) {
+      const int rho = e / HD, d = e - (e / HD) * HD;
+      float y = 0.f;
+      if (rho < nrows) {
+        const int r = rho / G, hq = h * G + (rho - r * G);
+        const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
+        const float x = bf2f(qr[d]);
+        if (trow && d < 2 * RH) {
+          const bool lo = d < RH;
+          const int i = lo ? d : d - RH;
+          const float xp = bf2f(qr[lo ? d + RH : d - RH]);
+          const float c = trow[i], s = sgn * trow[RH + i];
+          y = lo ? x * c - xp * s : x * c + xp * s;
+        } else {
+          y = x;
+        }
+        const __nv_bfloat16 yb = __float2bfloat16_rn(y);
+        if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
+        Qs[rho * C::QSTRIDE + d] = yb;
+      } else {
+        Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+  __syncthreads();  // barrier inits and the query tile are visible to every warp
+
+  // Warp roles.
+  const int mt = warp % MT, ng = warp / MT, nt_lo = ng * QNT;  // QK: key m-tile, n-tile group
+  const int hg = warp % C::HG, kg = warp / C::HG;                 // PV: hd group, key group
+  const int g4 = lane >> 2, t4 = lane & 3;
+
+  // Query fragments (B operand of S^T = K . Q^T) for this warp's n-tiles.
+  uint32_t qfr[C::Q_REGS ? QNT : 1][C::Q_REGS ? HD / 16 : 1][2];
+  const uint32_t qs_base = smem_u32(Qs);
+  if constexpr (C::Q_REGS) {
+#pragma unroll
+    for (int j = 0; j < QNT; ++j) {
+      const int nt = min(nt_lo + j, NT - 1);
+#pragma unroll
+      for (int kp = 0; kp < HD / 32; ++kp) {
+        const uint32_t a = qs_base + ((nt * 8 + (lane & 7)) * C::QSTRIDE + kp * 32 + (lane >> 3) * 8) * 2;
+        ldsm_x4(a, qfr[j][2 * kp][0], qfr[j][2 * kp][1], qfr[j][2 * kp + 1][0], qfr[j][2 * kp + 1][1]);
+      }
+    }
+  }
+
+  // Row limits of this thread's QK rows (global positions; 0 for padding rows).
+  int lim[QNT][2];
+#pragma unroll
+  for (int j = 0; j < QNT; ++j)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int rho = (nt_lo + j) * 8 + t4 * 2 + c;
+      lim[j][c] = (rho < nrows && nt_lo + j < NT) ? static_cast<int>(min64(lim_base + rho / G, end)) : 0;
+    }
+
+  float oacc[PV_MT][NT][4];
+#pragma unroll
+  for (int a = 0; a < PV_MT; ++a)
+#pragma unroll
+    for (int b = 0; b < NT; ++b) oacc[a][b][0] = oacc[a][b][1] = oacc[a][b][2] = oacc[a][b][3] = 0.f;
+  // Row maxima (log2 domain) of all rows this thread touches in PV; with NG > 1 the QK rows are a
+  // subset kept separately (same values, computed from the same shared data).
+  float mrow[NT][2], mq_own[NG == 1 ? 1 : QNT][2], lq[QNT][2];
+#pragma unroll
+  for (int b = 0; b < NT; ++b) mrow[b][0] = mrow[b][1] = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < (NG == 1 ? 1 : QNT); ++j) mq_own[j][0] = mq_own[j][1] = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < QNT; ++j) lq[j][0] = lq[j][1] = 0.f;
+  auto MQ = [&](int j, int c) -> float& {
+    if constexpr (NG == 1) return mrow[j][c];
+    else return mq_own[j][c];
+  };
+
+  bool timed_out = false;
+  int consumed = 0;
+  const uint32_t p_base = smem_u32(smem + C::OFF_P);
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int st = it % NSTAGE;
+    const bool ok = mbar_wait(&full[st], (it / NSTAGE) & 1);
+    const uint32_t kv_base = smem_u32(smem + st * C::STAGE_BYTES);
+    const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
+    const int64_t key0 = p.pos_lo + static_cast<int64_t>(t_begin + it) * TK + mt * 16 + g4;
+
+    float x[QNT][4];
+    float ls[QNT][2];
+    bool exceed = false;
+#pragma unroll
+    for (int j = 0; j < QNT; ++j) x[j][0] = x[j][1] = x[j][2] = x[j][3] = 0.f, ls[j][0] = ls[j][1] = 0.f;
+    if (ok) {
+      // ---- S^T = K . Q^T for keys [mt*16, mt*16+16) of the tile
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const int row = mt * 16 + (lane & 15);
+        const int chunk = (kk & 3) * 2 + (lane >> 4);
+        const uint32_t a = kv_base + (kk >> 2) * C::BOX_BYTES + row * 128 + ((chunk ^ (row & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(a, a0, a1, a2, a3);
+#pragma unroll
+        for (int j = 0; j < QNT; ++j) {
+          if (nt_lo + j < NT) {
+            uint32_t b0, b1;
+            if constexpr (C::Q_REGS) {
+              b0 = qfr[j][kk][0];
+              b1 = qfr[j][kk][1];
+            } else {
+              const uint32_t qa =
+                  qs_base + (((nt_lo + j) * 8 + (lane & 7)) * C::QSTRIDE + kk * 16 + ((lane >> 3) & 1) * 8) * 2;
+              ldsm_x2(qa, b0, b1);
+            }
+            mma_bf16(x[j], a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+      // ---- scale, mask, exponentiate against the current row maximum
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = e & 1;
+          const int64_t key = key0 + (e >> 1) * 8;
+          const float v = key < lim[j][c] ? x[j][e] * p.scale_log2 : -INFINITY;
+          x[j][e] = v;
+          exceed |= v > MQ(j, c) + kRaise;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+        const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
+        const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
+        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+        ls[j][0] = p0 + p2;
+        ls[j][1] = p1 + p3;
+        if (nt_lo + j < NT) {
+          const int r0 = (nt_lo + j) * 8 + t4 * 2;
+          const int k0 = mt * 16 + g4;
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p2, p3)));
+        }
+      }
+    }
+
+    // One barrier per tile: P^T of every warp is written, every warp is done with the previous
+    // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
+    const bool attention = named_bar_or(exceed || !ok, 1, NTH);
+    if (tid == 0 && it >= 1 && it - 1 + NSTAGE < ntiles)
+      issue_tile<C>(smem, full, &map, (it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE, p.hkv, h, pol);
+    if (attention) {
+      if (named_bar_or(!ok, 2, NTH)) {
+        timed_out = true;
+        if (lane == 0) set_error(p.err, FOLD_DEVERR_TIMEOUT);
+        break;
+      }
+      // ---- raise the row maximum where a logit passed it by more than 2^kRaise
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v = fmaxf(x[j][c], x[j][c + 2]);
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+          if (lane < 4 && nt_lo + j < NT) red[mt * ROWS + (nt_lo + j) * 8 + lane * 2 + c] = v;
+        }
+      }
+      named_bar_sync(2, NTH);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int row = nt * 8 + t4 * 2 + c;
+          float tm = red[row];
+#pragma unroll
+          for (int q = 1; q < MT; ++q) tm = fmaxf(tm, red[q * ROWS + row]);
+          const float mo = mrow[nt][c];
+          const float mn = tm > mo + kRaise ? tm : mo;
+          const float f = mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
+          mrow[nt][c] = mn;
+#pragma unroll
+          for (int a = 0; a < PV_MT; ++a) {
+            oacc[a][nt][c] *= f;
+            oacc[a][nt][c + 2] *= f;
+          }
+          if constexpr (NG == 1) {
+            lq[nt][c] *= f;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+        if constexpr (NG > 1) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int row = min(nt_lo + j, NT - 1) * 8 + t4 * 2 + c;
+            float tm = red[row];
+#pragma unroll
+            for (int q = 1; q < MT; ++q) tm = fmaxf(tm, red[q * ROWS + row]);
+            const float mo = mq_own[j][c];
+            const float mn = tm > mo + kRaise ? tm : mo;
+            lq[j][c] *= mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
+            mq_own[j][c] = mn;
+          }
+        }
+        const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
+        const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
+        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+        ls[j][0] = p0 + p2;
+        ls[j][1] = p1 + p3;
+        if (nt_lo + j < NT) {
+          const int r0 = (nt_lo + j) * 8 + t4 * 2;
+          const int k0 = mt * 16 + g4;
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p2, p3)));
+        }
+      }
+      named_bar_sync(2, NTH);
+    }
+#pragma unroll
+    for (int j = 0; j < QNT; ++j) lq[j][0] += ls[j][0], lq[j][1] += ls[j][1];
+
+    // ---- O^T += V^T . P^T over this warp's hd group and key group
+#pragma unroll
+    for (int ks = 0; ks < C::PV_KS; ++ks) {
+      const int kk = kg * C::PV_KS + ks;
+      uint32_t bfr[NT][2];
+#pragma unroll
+      for (int nt = 0; nt + 1 < NT; nt += 2) {
+        const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        const int col = (nt + (lane >> 4)) * 8;
+        ldsm_x4_t(pt + (key * C::PSTRIDE + col) * 2, bfr[nt][0], bfr[nt][1], bfr[nt + 1][0], bfr[nt + 1][1]);
+      }
+      if constexpr (NT & 1) {
+        const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        ldsm_x2_t(pt + (key * C::PSTRIDE + (NT - 1) * 8) * 2, bfr[NT - 1][0], bfr[NT - 1][1]);
+      }
+#pragma unroll
+      for (int a = 0; a < PV_MT; ++a) {
+        const int ht = hg * PV_MT + a;
+        const int q = lane >> 3;
+        const int key_row = kk * 16 + (q >> 1) * 8 + (lane & 7);
+        const int chunk = (ht & 3) * 2 + (q & 1);
+        const uint32_t va =
+            kv_base + (C::KBOX + (ht >> 2)) * C::BOX_BYTES + key_row * 128 + ((chunk ^ (key_row & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(va, a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16(oacc[a][nt], a0, a1, a2, a3, bfr[nt][0], bfr[nt][1]);
+      }
+    }
+    consumed = it + 1;
+  }
+
+  // -------------------------------------------------------------- epilogue
+  const int64_t o_split = static_cast<int64_t>(split) * p.n * p.hq * HD;
+  const int64_t l_split = static_cast<int64_t>(split) * p.hq * p.n;
+  if (timed_out) {
+    // Copies still in flight must land before this CTA's shared memory is released.
+    if (tid == 0) {
+      const int issued = min(ntiles, max(consumed, 1) - 1 + NSTAGE);
+      for (int i = consumed; i < issued; ++i)
+        if (!mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1)) break;
+    }
+    for (int e = tid; e < nrows * HD; e += NTH) {
+      const int rho = e / HD, d = e - rho * HD;
+      const int r = rho / G, hq = h * G + (rho - r * G);
+      p.o_part[o_split + (static_cast<int64_t>(r) * p.hq + hq) * HD + d] = 0.f;
+      if (d == 0) p.lse_part[l_split + static_cast<int64_t>(hq) * p.n + r] = -INFINITY;
+    }
+    return;
+  }
+  // row sums: lanes sharing t4 hold the same rows
+#pragma unroll
+  for (int j = 0; j < QNT; ++j)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float v = lq[j][c];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (lane < 4 && nt_lo + j < NT) red[mt * ROWS + (nt_lo + j) * 8 + lane * 2 + c] = v;
+    }
+  if (warp == 0 && lane < 4) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) row_m[nt * 8 + lane * 2] = mrow[nt][0], row_m[nt * 8 + lane * 2 + 1] = mrow[nt][1];
+  }
+  // every copy has landed and been consumed: the stage memory holds the O reduction
+  float* ored = reinterpret_cast<float*>(smem);
+#pragma unroll
+  for (int kgi = 0; kgi < C::KG; ++kgi) {
+    __syncthreads();
+    if (kg == kgi) {
+#pragma unroll
+      for (int a = 0; a < PV_MT; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = (hg * PV_MT + a) * 16 + g4 + (e >> 1) * 8;
+            const int row = nt * 8 + t4 * 2 + (e & 1);
+            float* o = ored + row * HD + d;
+            *o = kgi == 0 ? oacc[a][nt][e] : *o + oacc[a][nt][e];
+          }
+    }
+  }
+  __syncthreads();
+  if (tid < ROWS) {
+    float L = 0.f;
+#pragma unroll
+    for (int q = 0; q < MT; ++q) L += red[q * ROWS + tid];
+    const float m = row_m[tid];
+    row_inv[tid] = L > 0.f ? 1.f / L : 0.f;
+    if (tid < nrows) {
+      const int r = tid / G, hq = h * G + (tid - r * G);
+      p.lse_part[l_split + static_cast<int64_t>(hq) * p.n + r] = L > 0.f ? (m + __log2f(L)) * kLn2 : -INFINITY;
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < nrows * (HD / 4); e += NTH) {
+    const int rho = e / (HD / 4), d4 = e - rho * (HD / 4);
+    const int r = rho / G, hq = h * G + (rho - r * G);
+    const float s = row_inv[rho];
+    float4 v = reinterpret_cast<const float4*>(ored + rho * HD)[d4];
+    v.x *= s, v.y *= s, v.z *= s, v.w *= s;
+    reinterpret_cast<float4*>(p.o_part + o_split + (static_cast<int64_t>(r) * p.hq + hq) * HD)[d4] = v;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+template <class C>
+int launch_far(const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
+  CUtensorMap map;
+  if (int s = side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)) return s;
+  auto kern = far_read_kernel<C>;
+  static bool configured = false;  // per instantiation
+  if (!configured) {
+    if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                           "cudaFuncSetAttribute(far_read)"))
+      return s;
+    configured = true;
+  }
+  dim3 grid(prm.splits, prm.hkv);
+  kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(map, prm);
+  return check_launch("far_read_kernel");
+}
+
+template <int HD, int TK, int HG>
+int dispatch_nt(int nt, const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
+  switch (nt) {
+    case 1: return launch_far<FarCfg<HD, 1, TK, HG>>(prm, side, pages, stream);
+    case 2: return launch_far<FarCfg<HD, 2, TK, HG>>(prm, side, pages, stream);
+    case 3: return launch_far<FarCfg<HD, 3, TK, HG>>(prm, side, pages, stream);
+    case 4: return launch_far<FarCfg<HD, 4, TK, HG>>(prm, side, pages, stream);
+    case 5: return launch_far<FarCfg<HD, 5, TK, HG>>(prm, side, pages, stream);
+    case 6: return launch_far<FarCfg<HD, 6, TK, HG>>(prm, side, pages, stream);
+    case 7: return launch_far<FarCfg<HD, 7, TK, HG>>(prm, side, pages, stream);
+    case 8: return launch_far<FarCfg<HD, 8, TK, HG>>(prm, side, pages, stream);
+    default: return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
+  }
+}
+
+}  // namespace fold
+
+extern "C" {
+
+int fold_far_read_default_splits(int hkv, int hd, int n, int hq) {
+  (void)hd, (void)n, (void)hq;
+  int sms = fold::device_sm_count();
+  if (sms <= 0) sms = 148;
+  if (hkv <= 0) return 1;
+  return std::max(1, sms / hkv);
+}
+
+int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,
+                  const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
+                  int64_t capacity, int* far_len, void* qf, int64_t qf_stride_tok, int64_t qf_stride_head,
+                  float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd, int window, int block,
+                  int far_distance, float softmax_scale, int* err, void* stream) {
+  using namespace fold;
+  if (!q || !qsl || !seq_lens || !side || !o_part || !lse_part)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: null pointer");
+  if (n < 1 || hq < 1 || hkv < 1 || hq % hkv || splits < 1 || pages < 2 || window < 1 || block < 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: bad sizes (n, hq, hkv, splits, pages, window, block)");
+  if (splits > 65535) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: too many splits");
+  if (hd != 128 && hd != 256) return fail(FOLD_ERR_UNSUPPORTED, "far read: head size must be 128 or 256");
+  if (rope_table && (rot_dim < 2 || rot_dim % 2 || rot_dim > hd || table_rows < 1))
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: bad rotary size or table");
+  if (pos_lo < 0 || pos_lo % 256) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: pos_lo must be a multiple of 256");
+  if (static_cast<int64_t>(pages) * hkv > (1ll << 31) - 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: side cache too large for one descriptor");
+  const int rows = n * (hq / hkv);
+  if (rows > 64) return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
+  FarParams prm{};
+  prm.q = static_cast<const __nv_bfloat16*>(q);
+  prm.q_st = q_stride_tok, prm.q_sh = q_stride_head;
+  prm.qsl = qsl, prm.seq = seq_lens;
+  prm.table = rope_table, prm.table_rows = table_rows, prm.rot_dim = rot_dim;
+  prm.pos_lo = pos_lo, prm.capacity = capacity, prm.local_cap = static_cast<int64_t>(pages - 1) * 256;
+  prm.far_len = far_len;
+  prm.qf = static_cast<__nv_bfloat16*>(qf), prm.qf_st = qf_stride_tok, prm.qf_sh = qf_stride_head;
+  prm.o_part = o_part, prm.lse_part = lse_part;
+  prm.splits = splits, prm.n = n, prm.hq = hq, prm.hkv = hkv, prm.group = hq / hkv;
+  prm.window = window, prm.block = block, prm.far_distance = far_distance;
+  prm.scale_log2 = softmax_scale * kLog2e;
+  prm.err = err;
+  const int nt = (rows + 7) / 8;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (hd == 128) return dispatch_nt<128, 128, 4>(nt, prm, side, pages, s);
+  return dispatch_nt<256, 64, 8>(nt, prm, side, pages, s);
+}
+
+}  // extern "C"

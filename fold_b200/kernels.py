@@ -1,0 +1,194 @@
+"""Python face of the CUDA kernels, with the reference's kernel API (fold/kernels.py:111-142).
+
+far_query, rerope_queries and merge keep the reference's names, arguments and results. far_read,
+append, gather and combine are the new entry points that replace the FlashAttention read of the
+side cache and its torch scatter. All of them run on the current CUDA stream, read the step
+lengths on the device (graph-capturable) and raise FoldError when the library reports an error.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from .errors import FoldError
+from .rope import rope_table
+
+SIDE_BLOCK = 256  # positions per side-cache page (fold/attention.py:48)
+DEFAULT_TABLE_ROWS = 1 << 18
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise FoldError("FOLD kernels take CUDA tensors (there is no CPU path)")
+
+
+def _check_lengths(qsl, seq_lens):
+    if qsl.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise FoldError("query_start_loc and seq_lens must be int32")
+
+
+def _table_for(inv_freq, device, rows):
+    return rope_table(inv_freq, rows, device)
+
+
+def far_query(q, qsl, seq_lens, inv_freq, far_len, *, far_distance, window, block, table=None):
+    """q [n, Hq, D] -> far query [n, Hq, D] rotated by (D - H) * inv_freq. Writes far_len[0].
+    (fold/kernels.py:111-119). `table` is an optional prebuilt rope table."""
+    _require_cuda(q, qsl, seq_lens, far_len)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = q.shape
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if table is None:
+        table = _table_for(inv_freq, q.device, DEFAULT_TABLE_ROWS + int(far_distance) + 1)
+    qf = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
+    _lib.call("fold_far_query", _p(q), q.stride(0), q.stride(1), _p(qf), qf.stride(0), qf.stride(1), _p(qsl),
+              _p(seq_lens), _p(table), table.shape[0], table.shape[1], _p(far_len), n, hq, d, int(window), int(block),
+              int(far_distance), None, _stream(q))
+    return qf
+
+
+def rerope_queries(q, qsl, seq_lens, inv_freq, far_len, *, far_distance, window, block, constant, logn_ref,
+                   table=None):
+    """q [n, Hq, D] -> (window query, far query) for the ReRoPE baseline. Writes far_len[0].
+    (fold/kernels.py:122-132)."""
+    _require_cuda(q, qsl, seq_lens, far_len)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = q.shape
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if table is None:
+        table = _table_for(inv_freq, q.device, DEFAULT_TABLE_ROWS + int(far_distance) + n + 1)
+    qs = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
+    qf = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
+    inv_log_ref = (1.0 / math.log(logn_ref)) if logn_ref else 0.0
+    _lib.call("fold_rerope_query", _p(q), q.stride(0), q.stride(1), _p(qs), qs.stride(0), qs.stride(1), _p(qf),
+              qf.stride(0), qf.stride(1), _p(qsl), _p(seq_lens), _p(table), table.shape[0], table.shape[1],
+              _p(far_len), n, hq, d, int(window), int(block), int(far_distance), int(bool(constant)),
+              float(inv_log_ref), None, _stream(q))
+    return qs, qf
+
+
+def merge(out_l, lse_l, out_f, lse_f, out, qsl, seq_lens, *, window, block, alpha):
+    """Writes the mass-weighted merge into out [n, Hq, D] (fold/kernels.py:135-142).
+
+    out_l [n, Hq, D] bf16, lse_l [Hq, n]. The far side is either one read, out_f [n, Hq, D]
+    (bf16 or float32) with lse_f [Hq, n], or the split partials of far_read, out_f
+    [S, n, Hq, D] float32 with lse_f [S, Hq, n], which are combined on the fly."""
+    _require_cuda(out_l, lse_l, out_f, lse_f, out, qsl, seq_lens)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = out_l.shape
+    if out_f.dim() == 3:
+        of_s, (of_t, of_h), splits = 0, out_f.stride()[:2], 1
+        lf_s, lf_h, lf_t = 0, lse_f.stride(0), lse_f.stride(1)
+    else:
+        splits = out_f.shape[0]
+        of_s, of_t, of_h = out_f.stride()[:3]
+        lf_s, lf_h, lf_t = lse_f.stride()
+    if out_f.stride(-1) != 1 or out_l.stride(-1) != 1 or out.stride(-1) != 1:
+        raise FoldError("merge: the head dimension must be contiguous")
+    if out_l.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise FoldError("merge: out_l and out must be bfloat16")
+    if out_f.dtype not in (torch.bfloat16, torch.float32) or lse_l.dtype != torch.float32 or lse_f.dtype != torch.float32:
+        raise FoldError("merge: out_f must be bf16/float32 and the LSEs float32")
+    _lib.call("fold_merge", _p(out_l), out_l.stride(0), out_l.stride(1), _p(lse_l), lse_l.stride(0), lse_l.stride(1),
+              _p(out_f), int(out_f.dtype == torch.bfloat16), of_s, of_t, of_h, _p(lse_f), lf_s, lf_h, lf_t, splits,
+              _p(out), out.stride(0), out.stride(1), _p(qsl), _p(seq_lens), n, hq, d, int(window), int(block),
+              1.0 / float(alpha), _stream(out))
+
+
+def far_read(q, qsl, seq_lens, side, o_part, lse_part, *, window, block, far_distance, softmax_scale,
+             table=None, rot_dim=None, far_len=None, qf=None, pos_lo=0, capacity=None, err=None):
+    """Split-KV read of the side cache with the far-query rotation fused in.
+
+    q [n, Hq, D] bf16, RoPE'd at positions H + r (or already the far query when table is None);
+    side [pages, Hkv, 256, 2D] bf16; o_part [S, n, Hq, D] and lse_part [S, Hq, n] float32 receive
+    one normalised partial per split. The cache holds positions [pos_lo, pos_lo + (pages-1)*256);
+    capacity (default: that range's end) bounds far_len for the capacity check."""
+    _require_cuda(q, qsl, seq_lens, side, o_part, lse_part, table, far_len, qf, err)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = q.shape
+    pages, hkv = side.shape[0], side.shape[1]
+    if side.dtype != torch.bfloat16 or q.dtype != torch.bfloat16:
+        raise FoldError("far_read: q and the side cache must be bfloat16")
+    if not side.is_contiguous() or side.shape[2] != SIDE_BLOCK or side.shape[3] != 2 * d:
+        raise FoldError("far_read: side cache must be a contiguous [pages, Hkv, 256, 2 * head_dim] tensor")
+    splits = o_part.shape[0]
+    if o_part.shape != (splits, n, hq, d) or lse_part.shape != (splits, hq, n) or not o_part.is_contiguous() \
+            or not lse_part.is_contiguous() or o_part.dtype != torch.float32 or lse_part.dtype != torch.float32:
+        raise FoldError("far_read: partials must be contiguous float32 [S, n, Hq, D] and [S, Hq, n]")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if capacity is None:
+        capacity = int(pos_lo) + (pages - 1) * SIDE_BLOCK
+    if table is not None and rot_dim is None:
+        rot_dim = table.shape[1]
+    _lib.call("fold_far_read", _p(q), q.stride(0), q.stride(1), _p(qsl), _p(seq_lens), _p(table),
+              0 if table is None else table.shape[0], 0 if table is None else int(rot_dim), _p(side), pages,
+              int(pos_lo), int(capacity), _p(far_len), _p(qf), 0 if qf is None else qf.stride(0),
+              0 if qf is None else qf.stride(1), _p(o_part), _p(lse_part), splits, n, hq, hkv, d, int(window),
+              int(block), int(far_distance), float(softmax_scale), _p(err), _stream(q))
+
+
+def append(k, v, positions, slots, side, *, pos_lo=0, skip_foreign=False, err=None):
+    """Writes K [ctx, Hkv, D] (before RoPE) and V [ctx, Hkv, D] of committed entries into the
+    side cache at their positions (fold/attention.py:260-265); rows with slot < 0 go to the
+    dummy slot. positions and slots are int64 (int32 inputs are widened)."""
+    _require_cuda(k, v, positions, slots, side, err)
+    ctx = k.shape[0]
+    if ctx == 0:
+        return
+    pages, hkv, _, d2 = side.shape
+    if k.dtype != side.dtype or v.dtype != side.dtype or side.dtype != torch.bfloat16:
+        raise FoldError("append: K, V and the side cache must be bfloat16")
+    if k.shape[1:] != (hkv, d2 // 2) or v.shape[1:] != (hkv, d2 // 2) or v.shape[0] < ctx:
+        raise FoldError("append: K/V must be [ctx, Hkv, head_dim] matching the side cache")
+    if k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise FoldError("append: the head dimension of K and V must be contiguous")
+    positions = positions[:ctx].to(torch.int64)
+    slots = slots[:ctx].to(torch.int64)
+    _lib.call("fold_append", _p(k), k.stride(0), k.stride(1), _p(v), v.stride(0), v.stride(1), _p(positions),
+              _p(slots), ctx, _p(side), pages, hkv, d2 // 2, int(pos_lo), int(bool(skip_foreign)), _p(err),
+              _stream(side))
+
+
+def gather(side, positions, *, pos_lo=0, err=None):
+    """K, V [m, Hkv, D] of the given absolute positions of a side cache."""
+    _require_cuda(side, positions, err)
+    pages, hkv, _, d2 = side.shape
+    positions = positions.to(torch.int64).contiguous()
+    m = positions.numel()
+    k = torch.empty((m, hkv, d2 // 2), device=side.device, dtype=side.dtype)
+    v = torch.empty_like(k)
+    _lib.call("fold_gather", _p(side), pages, hkv, d2 // 2, int(pos_lo), _p(positions), m, _p(k), _p(v), _p(err),
+              _stream(side))
+    return k, v
+
+
+def combine(o_part, lse_part, o_out=None, lse_out=None):
+    """Log-sum-exp combine of S partials [S, n, Hq, D] / [S, Hq, n] into one (float32)."""
+    _require_cuda(o_part, lse_part)
+    s, n, hq, d = o_part.shape
+    if o_out is None:
+        o_out = torch.empty((n, hq, d), device=o_part.device, dtype=torch.float32)
+    if lse_out is None:
+        lse_out = torch.empty((hq, n), device=o_part.device, dtype=torch.float32)
+    _lib.call("fold_combine", _p(o_part.contiguous()), _p(lse_part.contiguous()), s, _p(o_out), _p(lse_out), n, hq, d,
+              _stream(o_part))
+    return o_out, lse_out
+
+
+def default_splits(hkv):
+    """Split count per KV head that fills the device with one CTA per SM."""
+    return _lib.default_splits(hkv, 0, 0, 0)

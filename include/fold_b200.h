@@ -1,0 +1,134 @@
+/* C-ABI of the FOLD drafter-attention hot path on B200 (sm_100a).
+ *
+ * Every entry point takes plain device pointers (owned by the caller), sizes and strides in
+ * elements, and a CUDA stream (`stream`, a cudaStream_t passed as void*). None of them allocates
+ * device memory, synchronises the host or reads a device value on the host: the lengths of a
+ * draft step (query_start_loc, seq_lens) are read on the device, so every call can be captured
+ * in a CUDA graph. Each returns FOLD_OK (0) or a fold_status; fold_last_error() gives the detail
+ * of the last failure on the calling thread.
+ *
+ * Conventions (fold/kernels.py:1-13 of the reference): batch 1; qlen = qsl[1] - qsl[0];
+ * H = max(seq_lens[0] - qlen, 0) committed entries; W = window; B = block; D = far distance
+ * (W + B by default); far_len = max(0, H - W - B + qlen); row r reads the far keys
+ * [0, H - W - B + 1 + r). LSE arrays are natural logs laid out [Hq, n] like FlashAttention's;
+ * an empty row has lse = -inf and output 0.
+ *
+ * The side cache keeps the reference's layout side[pages, Hkv, 256, 2*hd] bf16, contiguous, keys
+ * before RoPE in [..., :hd] and values in [..., hd:] (fold/attention.py:48,64-66). The last page
+ * holds the dummy slot pages*256 - 1 that rows with an invalid slot are written to.
+ *
+ * Device error word: kernels OR FOLD_DEVERR_* bits into `err` (an int32 in device memory, may be
+ * NULL) instead of faulting; the caller reads it when convenient.
+ */
+#ifndef FOLD_B200_H_
+#define FOLD_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fold_status {
+  FOLD_OK = 0,
+  FOLD_ERR_INVALID_ARGUMENT = 1, /* a size, stride or option the kernels do not take */
+  FOLD_ERR_UNSUPPORTED = 2,      /* a head size / row count without a compiled kernel */
+  FOLD_ERR_ALIGNMENT = 3,        /* a pointer or stride breaks the 16-byte vector rule */
+  FOLD_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+  FOLD_ERR_TENSOR_MAP = 5        /* the TMA descriptor of the side cache could not be built */
+};
+
+#define FOLD_DEVERR_APPEND_RANGE 1 /* an append/gather position lies outside the cache */
+#define FOLD_DEVERR_ROPE_RANGE 2   /* |rotation offset| beyond the rope table (offset clamped) */
+#define FOLD_DEVERR_TIMEOUT 4      /* a pipeline wait of the far read gave up */
+#define FOLD_DEVERR_CAPACITY 8     /* far_len exceeds the side cache's capacity */
+
+const char* fold_status_string(int status);
+const char* fold_last_error(void);
+int fold_version(void);
+/* Number of streaming multiprocessors of the current device (0 if unknown). */
+int fold_num_sms(void);
+
+/* Side-cache append. Replaces the scatter of fold/attention.py:260-265
+ * (ws.side[pg, :, off, :hd] = raw; ws.side[pg, :, off, hd:] = v).
+ * k, v: [ctx, hkv, hd] bf16, innermost dim contiguous, strides (tok, head) in elements.
+ * positions, slots: int64[ctx]; a row with slot < 0 goes to the dummy slot pages*256 - 1.
+ * pos_lo: first absolute position this cache holds (0 unless the cache is a shard). A row whose
+ * position lies outside [pos_lo, pos_lo + (pages-1)*256) is skipped; it sets
+ * FOLD_DEVERR_APPEND_RANGE unless `skip_foreign` (a shard skips other ranks' positions). */
+int fold_append(const void* k, int64_t k_stride_tok, int64_t k_stride_head, const void* v, int64_t v_stride_tok,
+                int64_t v_stride_head, const int64_t* positions, const int64_t* slots, int ctx, void* side,
+                int pages, int hkv, int hd, int64_t pos_lo, int skip_foreign, int* err, void* stream);
+
+/* Read back K and V of absolute positions into k_out, v_out [m, hkv, hd] bf16 (contiguous).
+ * The inverse of fold_append for checks and shard moves; no reference counterpart beyond the
+ * FlashAttention page read of fold/attention.py:165. */
+int fold_gather(const void* side, int pages, int hkv, int hd, int64_t pos_lo, const int64_t* positions, int m,
+                void* k_out, void* v_out, int* err, void* stream);
+
+/* Far query. Replaces far_query / _far_query_kernel (fold/kernels.py:21-46,111-119): rotates the
+ * RoPE'd block queries q [n, hq, hd] by the angle (D - H) * inv_freq on the first rot_dim dims
+ * (neox halves), writes qf [n, hq, hd] bf16 and far_len[0] (may be NULL).
+ * rope_table: float32 [table_rows, rot_dim] holding cos(p f_i) then sin(p f_i) for p = 0.. (the
+ * layout of vLLM's cos_sin_cache), indexed by |D - H|. */
+int fold_far_query(const void* q, int64_t q_stride_tok, int64_t q_stride_head, void* qf, int64_t qf_stride_tok,
+                   int64_t qf_stride_head, const int* qsl, const int* seq_lens, const float* rope_table,
+                   int table_rows, int rot_dim, int* far_len, int n, int hq, int hd, int window, int block,
+                   int far_distance, int* err, void* stream);
+
+/* ReRoPE query pair. Replaces rerope_queries / _rerope_query_kernel (fold/kernels.py:49-83,
+ * 122-132): qs = q * max(1, log(H + t + 1) * inv_log_ref) when inv_log_ref > 0, else q;
+ * qf = qs rotated by (D - H) (minus t when `constant`). Writes far_len[0] (may be NULL). */
+int fold_rerope_query(const void* q, int64_t q_stride_tok, int64_t q_stride_head, void* qs, int64_t qs_stride_tok,
+                      int64_t qs_stride_head, void* qf, int64_t qf_stride_tok, int64_t qf_stride_head,
+                      const int* qsl, const int* seq_lens, const float* rope_table, int table_rows, int rot_dim,
+                      int* far_len, int n, int hq, int hd, int window, int block, int far_distance, int constant,
+                      float inv_log_ref, int* err, void* stream);
+
+/* Far-memory read with the far-query rotation fused in. Replaces the FlashAttention read of the
+ * side cache (fold/attention.py:164-170; causal bottom-right, seqused_k = far_len,
+ * softmax_scale = alpha * scale, num_splits) together with far_query (fold/attention.py:162).
+ * q: RoPE'd queries [n, hq, hd] bf16. With rope_table == NULL, q is used unrotated (it already
+ * is the far query, e.g. from fold_rerope_query). The cache holds positions
+ * [pos_lo, pos_lo + (pages-1)*256); `capacity` is the total number of positions all shards hold
+ * (FOLD_DEVERR_CAPACITY if far_len exceeds it). Each of `splits` CTAs per KV head reads a
+ * contiguous range of this cache's far keys and writes a partial (o, lse):
+ * o_part [splits, n, hq, hd] float32, lse_part [splits, hq, n] float32 (natural log of the sum of
+ * exp(softmax_scale * q.k)). far_len (may be NULL) and qf (may be NULL; [n, hq, hd] bf16 with the
+ * given strides) are also written. Supports hd in {128, 256}, rot_dim even <= hd,
+ * n * (hq / hkv) <= 64. */
+int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,
+                  const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
+                  int64_t capacity, int* far_len, void* qf, int64_t qf_stride_tok, int64_t qf_stride_head,
+                  float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd, int window, int block,
+                  int far_distance, float softmax_scale, int* err, void* stream);
+
+/* Split count that fills the device for `hkv` KV heads (one CTA per SM). */
+int fold_far_read_default_splits(int hkv, int hd, int n, int hq);
+
+/* LSE merge. Replaces merge / _merge_kernel (fold/kernels.py:86-108,135-142) and absorbs the
+ * split-KV combine: o_f holds `splits` far partials (float32 when of_bf16 == 0, else bf16) with
+ * strides (split, tok, head), lse_f their LSEs with strides (split, head, tok). Per row t and head:
+ * the far partials are combined by log-sum-exp, lf = lse_far * inv_alpha, and when
+ * H - W - B + 1 + t > 0 the output is (e^{ll-m} o_l + e^{lf-m} o_f) / (e^{ll-m} + e^{lf-m}),
+ * m = max(ll, lf); otherwise it is o_l. o_l [n, hq, hd] bf16, lse_l [hq, n] float32 with the
+ * given strides; out bf16 with strides (tok, head). */
+int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, const float* lse_l,
+               int64_t ll_stride_head, int64_t ll_stride_tok, const void* o_f, int of_bf16, int64_t of_stride_split,
+               int64_t of_stride_tok, int64_t of_stride_head, const float* lse_f, int64_t lf_stride_split,
+               int64_t lf_stride_head, int64_t lf_stride_tok, int splits, void* out, int64_t out_stride_tok,
+               int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd, int window,
+               int block, float inv_alpha, void* stream);
+
+/* Log-sum-exp combine of `splits` partials o_part [splits, n, hq, hd], lse_part [splits, hq, n]
+ * (float32, contiguous) into one partial o_out [n, hq, hd], lse_out [hq, n]. Used on each rank
+ * of a sharded far read before the partials are exchanged; no reference counterpart (the
+ * reference runs on one GPU; FlashAttention combines its splits internally). */
+int fold_combine(const float* o_part, const float* lse_part, int splits, float* o_out, float* lse_out, int n, int hq,
+                 int hd, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FOLD_B200_H_ */

@@ -72,6 +72,17 @@ BLOCK_CASES = [
 ]
 
 
+# Larger cases stored as (seed, shapes, sha256 of the inputs, output): the inputs regenerate from
+# numpy's default_rng. (name, seed, t, B, W, hq, hkv, d, rot, theta, alpha)
+REGEN_CASES = [
+    ("gqa4_h128", 41, 1500, 10, 256, 8, 2, 128, 128, 500000.0, 2.0),
+    ("gqa2_h256", 42, 900, 8, 128, 4, 2, 256, 256, 1e6, 2.0),
+    ("gqa4_h256_tail", 43, 300, 16, 280, 8, 2, 256, 256, 1e6, 2.0),   # only the last rows reach memory
+    ("qwen3_like", 44, 3000, 8, 512, 32, 8, 128, 128, 1e6, 2.0),
+    ("partial_rot_h128", 45, 700, 5, 100, 4, 1, 128, 64, 500000.0, 3.0),
+]
+
+
 def gen_fold_block(torch, ref, full):
     for name, seed, t, B, W, hq, hkv, d, rot, theta, alpha in BLOCK_CASES:
         q, kc, vc, kb, vb = block_inputs(seed, t, B, hq, hkv, d)
@@ -81,6 +92,15 @@ def gen_fold_block(torch, ref, full):
         np.savez_compressed(HERE / f"fold_block_{name}.npz", q=q, k_ctx=kc, v_ctx=vc, k_blk=kb, v_blk=vb,
                             inv_freq=f, window=W, alpha=alpha, scale=scale, out=out)
         print("fold_block", name, out.shape)
+    for name, seed, t, B, W, hq, hkv, d, rot, theta, alpha in REGEN_CASES:
+        q, kc, vc, kb, vb = block_inputs(seed, t, B, hq, hkv, d)
+        f = inv_freq(theta, rot)
+        scale = d ** -0.5
+        out = run_fold_block(torch, ref, q, kc, vc, kb, vb, window=W, alpha=alpha, freq=f, scale=scale)
+        np.savez_compressed(HERE / f"fold_block_regen_{name}.npz", seed=seed, t=t, B=B, hq=hq, hkv=hkv, d=d,
+                            rot=rot, theta=theta, window=W, alpha=alpha, scale=scale,
+                            inputs_sha256=sha(q, kc, vc, kb, vb), out=out)
+        print("fold_block regen", name, out.shape)
     if full:
         # config 1: batch 1, 32 q / 8 kv heads, hd 128, B 10, t 8192, W 2048, alpha 2, theta 5e5, seed 0
         q, kc, vc, kb, vb = block_inputs(0, 8192, 10, 32, 8, 128)

@@ -1,0 +1,54 @@
+"""The C-ABI library loads without a GPU and exports every entry point include/fold_b200.h
+declares; the Python binding declares the same set. No kernel is launched."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from fold_b200 import _lib
+from fold_b200.errors import FoldError
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "fold_b200.h"
+
+
+def declared():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fold_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for required in ("fold_append", "fold_far_query", "fold_far_read", "fold_merge", "fold_combine",
+                     "fold_rerope_query", "fold_gather"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert sorted(_lib.SIGNATURES) == declared()
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.fold_version() >= 1
+    assert lib.fold_status_string(0) == b"ok"
+    assert lib.fold_status_string(3) == b"misaligned pointer or stride"
+
+
+def test_argument_errors_are_reported_without_a_gpu():
+    # invalid sizes are rejected before any CUDA call
+    with pytest.raises(FoldError, match="far read"):
+        _lib.call("fold_far_read", None, 0, 0, None, None, None, 0, 0, None, 0, 0, 0, None, None, 0, 0, None, None,
+                  1, 1, 1, 1, 128, 1, 1, 1, 1.0, None, None)
+    with pytest.raises(FoldError, match="merge"):
+        _lib.call("fold_merge", None, 0, 0, None, 0, 0, None, 0, 0, 0, 0, None, 0, 0, 0, 1, None, 0, 0, None, None,
+                  1, 1, 128, 1, 1, 0.5, None)
+    # an empty append is a no-op that needs no device
+    _lib.call("fold_append", None, 0, 0, None, 0, 0, None, None, 0, None, 2, 1, 128, 0, 0, None, None)

@@ -1,0 +1,104 @@
+"""The FOLD forward (FoldAttention.forward with the reference's signature) and the side-cache
+append path, on the GPU, against the reference's own fold_block outputs (tests/golden).
+
+The window read is a float32 torch stand-in for FlashAttention (it is outside the kernels of this
+package); the far read, the rotation, the merge and the append are the CUDA library."""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from fold_b200.attention import FoldAttention, FoldWorkspace, SlidingFoldAttention
+from oracle import fold_oracle as fo
+from tests.helpers import OUT_ATOL, bf16_tensor, golden_block_case, golden_block_names, torch_local_read
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+
+def build_step(g, device="cuda", sliding=False):
+    """Buffers of one draft step for a golden case: RoPE'd query and local cache, side cache
+    filled through the append kernel (keys before RoPE), fake vLLM layer and metadata."""
+    q, kc, vc, kb, vb = g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"]
+    t, B = kc.shape[0], q.shape[0]
+    hq, hkv, d = q.shape[1], kc.shape[1], q.shape[2]
+    f = g["inv_freq"]
+    keys = np.concatenate((kc, kb))
+    vals = np.concatenate((vc, vb))
+    k_roped = fo.rotate(keys, np.arange(t + B), f)
+    q_roped = fo.rotate(q, np.arange(t, t + B), f)
+    kv_cache = torch.stack((bf16_tensor(k_roped, device), bf16_tensor(vals, device)), dim=1)  # [seq, 2, hkv, d]
+    dummy_cache = torch.zeros((1, hkv, 16, 2 * d), device=device, dtype=torch.bfloat16)
+    W = g["window"]
+    inv = torch.from_numpy(f).to(device)
+    native = W + B - 1  # a sliding layer whose native causal window equals the FOLD window
+    ws = FoldWorkspace(dummy_cache, native + 1 - B if sliding else W, B, t + B, inv_freq=inv, far_distance=W + B,
+                       alpha=g["alpha"], num_heads=hq)
+    pos = torch.arange(t, device=device)
+    ws.append(bf16_tensor(kc, device), bf16_tensor(vc, device), pos, pos)
+    original = SimpleNamespace(head_size=d, scale=g["scale"], num_heads=hq, sliding_window=(native, 0),
+                               vllm_flash_attn_version=4)
+    meta = SimpleNamespace(num_actual_tokens=B, query_start_loc=torch.tensor([0, B], dtype=torch.int32, device=device),
+                           seq_lens=torch.tensor([t + B], dtype=torch.int32, device=device), max_query_len=B,
+                           max_seq_len=t + B, block_table=None, use_cascade=False, causal=True)
+    query = bf16_tensor(q_roped, device)
+    output = torch.empty((B, hq * d), device=device, dtype=torch.bfloat16)
+    return ws, original, meta, query, kv_cache, output
+
+
+CASES = golden_block_names(min_hd=128)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_fold_forward_matches_reference(name):
+    g = golden_block_case(name)
+    ws, original, meta, query, kv_cache, output = build_step(g)
+    layer = FoldAttention(original, ws, local_read=torch_local_read)
+    out = layer.forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    ws.check()
+    got = out.float().cpu().numpy().reshape(g["out"].shape)
+    assert np.abs(got - g["out"]).max() <= OUT_ATOL
+
+
+@pytest.mark.parametrize("name", CASES[:3])
+def test_sliding_fold_forward_matches_reference(name):
+    """sliding_layers="fold": native causal window (W + B - 1, 0) as the local branch."""
+    g = golden_block_case(name)
+    ws, original, meta, query, kv_cache, output = build_step(g, sliding=True)
+    layer = SlidingFoldAttention(original, ws, local_read=torch_local_read)
+    out = layer.forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    # with the native window W + B - 1 the native read sees the same near set as FOLD, except the
+    # block entries after each row (causal): compare against the oracle of that split
+    q, kc, vc, kb, vb = g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"]
+    t, B = kc.shape[0], q.shape[0]
+    f = g["inv_freq"]
+    keys = np.concatenate((kc, kb)).astype(np.float64)
+    vals = np.concatenate((vc, vb)).astype(np.float64)
+    k_roped = fo.bf16_round(fo.rotate(keys, np.arange(t + B), f))
+    q_roped = fo.bf16_round(fo.rotate(q, np.arange(t, t + B), f))
+    W = g["window"]
+    o_l, lse_l = fo.local_read(q_roped, k_roped, fo.bf16_round(vals), t, W + B - 1, 1, g["scale"])
+    qf = fo.far_query(q_roped, t, f, W + B)
+    lim = fo.far_row_limits(t, W, B, B)
+    o_f, lse_f = fo.far_read(qf, fo.bf16_round(keys[:t]), fo.bf16_round(vals[:t]), lim, g["scale"] * g["alpha"])
+    want = fo.merge(o_l, lse_l, o_f, lse_f, t, W, B, g["alpha"])
+    got = out.float().cpu().numpy().reshape(want.shape)
+    assert np.abs(got - want).max() <= OUT_ATOL
+
+
+def test_window_mode_and_empty_step():
+    g = golden_block_case(CASES[0])
+    ws, original, meta, query, kv_cache, output = build_step(g)
+    ws.mode = "window"
+    layer = FoldAttention(original, ws, local_read=torch_local_read)
+    out = layer.forward(None, query, None, None, kv_cache, meta, output)
+    o_l, _ = torch_local_read(query, kv_cache, meta, original, window_size=(ws.window + ws.block - 1,
+                                                                             ws.block - 1), causal=False, num_splits=1)
+    assert torch.equal(out, o_l.reshape(out.shape))
+    meta.num_actual_tokens = 0
+    assert torch.count_nonzero(layer.forward(None, query, None, None, kv_cache, meta, output)) == 0

@@ -15,7 +15,18 @@ def load(name):
     return dict(np.load(GOLDEN / name))
 
 
-BLOCK_CASES = sorted(p.name for p in GOLDEN.glob("fold_block_*.npz") if "config1" not in p.name)
+BLOCK_CASES = sorted(p.name for p in GOLDEN.glob("fold_block_*.npz") if "config1" not in p.name
+                     and "regen" not in p.name)
+REGEN_CASES = sorted(p.name for p in GOLDEN.glob("fold_block_regen_*.npz"))
+
+
+@pytest.mark.parametrize("name", REGEN_CASES)
+def test_regenerated_cases_match_reference(name):
+    from tests.helpers import golden_block_case
+    g = golden_block_case(name)
+    out = fo.fold_block(g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"], window=g["window"],
+                        alpha=g["alpha"], inv_freq=g["inv_freq"], scale=g["scale"])
+    np.testing.assert_allclose(out, g["out"], rtol=0, atol=1e-11)
 
 
 @pytest.mark.parametrize("name", BLOCK_CASES)
