@@ -33,6 +33,9 @@ SIGNATURES = {
     "fold_merge": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp,
                    _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp],
     "fold_combine": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp],
+    "fold_far_read_merge_static": [_vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp, _i64,
+                                   _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                   _i32, _f32, _f32, _vp, _vp],
 }
 _RESTYPES = {"fold_status_string": ctypes.c_char_p, "fold_last_error": ctypes.c_char_p}
 

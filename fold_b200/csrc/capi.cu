@@ -93,6 +93,24 @@ int side_tensor_map(const void* side, int pages, int hkv, int hd, int box_rows, 
   return FOLD_OK;
 }
 
+int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out) {
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    if (int s = load_encode()) return s;
+  }
+  if (!aligned16(side)) return fail(FOLD_ERR_ALIGNMENT, "side cache pointer is not 16-byte aligned");
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(2 * hd), 256u,
+                              static_cast<cuuint64_t>(pages) * static_cast<cuuint64_t>(hkv)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(2 * hd) * 2u, static_cast<cuuint64_t>(256 * 2 * hd) * 2u};
+  const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_rows), 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(side), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FOLD_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled failed");
+  return FOLD_OK;
+}
+
 }  // namespace fold
 
 extern "C" {

@@ -522,6 +522,72 @@ int dispatch_nt(int nt, const FarParams& prm, const void* side, int pages, cudaS
   }
 }
 
+template <class C>
+int launch_far_uncached(const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
+  CUtensorMap map;
+  if (int s = side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map)) return s;
+  auto kern = far_read_kernel<C>;
+  static bool configured = false;  // per instantiation
+  if (!configured) {
+    if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                           "cudaFuncSetAttribute(far_read)"))
+      return s;
+    configured = true;
+  }
+  kern<<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
+  return check_launch("far_read_kernel");
+}
+
+template <int HD, int TK, int HG>
+int dispatch_nt_uncached(int nt, const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
+  switch (nt) {
+    case 1: return launch_far_uncached<FarCfg<HD, 1, TK, HG>>(prm, side, pages, stream);
+    case 2: return launch_far_uncached<FarCfg<HD, 2, TK, HG>>(prm, side, pages, stream);
+    case 3: return launch_far_uncached<FarCfg<HD, 3, TK, HG>>(prm, side, pages, stream);
+    case 4: return launch_far_uncached<FarCfg<HD, 4, TK, HG>>(prm, side, pages, stream);
+    case 5: return launch_far_uncached<FarCfg<HD, 5, TK, HG>>(prm, side, pages, stream);
+    case 6: return launch_far_uncached<FarCfg<HD, 6, TK, HG>>(prm, side, pages, stream);
+    case 7: return launch_far_uncached<FarCfg<HD, 7, TK, HG>>(prm, side, pages, stream);
+    case 8: return launch_far_uncached<FarCfg<HD, 8, TK, HG>>(prm, side, pages, stream);
+    default: return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
+  }
+}
+
+int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                      const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side,
+                      int pages, int64_t pos_lo, int64_t capacity, int* far_len, float* o_part, float* lse_part,
+                      int splits, int n, int hq, int hkv, int hd, int window, int block, int far_distance,
+                      float softmax_scale, int* err, cudaStream_t stream) {
+  if (!q || !qsl || !seq_lens || !side || !o_part || !lse_part)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: null pointer");
+  if (n < 1 || hq < 1 || hkv < 1 || hq % hkv || splits < 1 || pages < 2 || window < 1 || block < 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: bad sizes (n, hq, hkv, splits, pages, window, block)");
+  if (splits > 65535) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: too many splits");
+  if (hd != 128 && hd != 256) return fail(FOLD_ERR_UNSUPPORTED, "far read: head size must be 128 or 256");
+  if (rope_table && (rot_dim < 2 || rot_dim % 2 || rot_dim > hd || table_rows < 1))
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: bad rotary size or table");
+  if (pos_lo < 0 || pos_lo % 256) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: pos_lo must be a multiple of 256");
+  if (static_cast<int64_t>(pages) * hkv > (1ll << 31) - 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: side cache too large for one descriptor");
+  const int rows = n * (hq / hkv);
+  if (rows > 64) return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
+  FarParams prm{};
+  prm.q = static_cast<const __nv_bfloat16*>(q);
+  prm.q_st = q_stride_tok, prm.q_sh = q_stride_head;
+  prm.qsl = qsl, prm.seq = seq_lens;
+  prm.table = rope_table, prm.table_rows = table_rows, prm.rot_dim = rot_dim;
+  prm.pos_lo = pos_lo, prm.capacity = capacity, prm.local_cap = static_cast<int64_t>(pages - 1) * 256;
+  prm.far_len = far_len;
+  prm.o_part = o_part, prm.lse_part = lse_part;
+  prm.splits = splits, prm.n = n, prm.hq = hq, prm.hkv = hkv, prm.group = hq / hkv;
+  prm.window = window, prm.block = block, prm.far_distance = far_distance;
+  prm.scale_log2 = softmax_scale * kLog2e;
+  prm.err = err;
+  const int nt = (rows + 7) / 8;
+  if (hd == 128) return dispatch_nt_uncached<128, 128, 4>(nt, prm, side, pages, stream);
+  return dispatch_nt_uncached<256, 64, 8>(nt, prm, side, pages, stream);
+}
+
 }  // namespace fold
 
 extern "C" {

@@ -26,6 +26,25 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // swizzle. Descriptors are cached per (pointer, shape, box).
 int side_tensor_map(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out);
 
+// The same descriptor, encoded into *out on every call without touching the cache (no heap use).
+int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out);
+
 int device_sm_count();
+
+// Far read into caller-given partial buffers with the descriptor built on the stack; the
+// arguments and checks are those of fold_far_read.
+int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                      const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side,
+                      int pages, int64_t pos_lo, int64_t capacity, int* far_len, float* o_part, float* lse_part,
+                      int splits, int n, int hq, int hkv, int hd, int window, int block, int far_distance,
+                      float softmax_scale, int* err, cudaStream_t stream);
+
+// Merge of contiguous float32 split partials [splits, n, hq, hd] / [splits, hq, n] with the window
+// read; the arguments of fold_merge for that partial layout.
+int merge_contiguous_partials(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, const float* lse_l,
+                              int64_t ll_stride_head, int64_t ll_stride_tok, const float* o_part,
+                              const float* lse_part, int splits, void* out, int64_t out_stride_tok,
+                              int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd,
+                              int window, int block, float inv_alpha, cudaStream_t stream);
 
 }  // namespace fold

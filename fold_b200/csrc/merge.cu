@@ -159,6 +159,30 @@ static int merge_launch(const MergeParams& p, int hd, bool combine, cudaStream_t
   return check_launch(combine ? "combine_kernel" : "merge_kernel");
 }
 
+int merge_contiguous_partials(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, const float* lse_l,
+                              int64_t ll_stride_head, int64_t ll_stride_tok, const float* o_part,
+                              const float* lse_part, int splits, void* out, int64_t out_stride_tok,
+                              int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd,
+                              int window, int block, float inv_alpha, cudaStream_t stream) {
+  if (!o_l || !lse_l || !o_part || !lse_part || !out || !qsl || !seq_lens)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "merge: null pointer");
+  if (n < 1 || hq < 1 || splits < 1) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge: bad sizes");
+  if (ol_stride_tok % 2 || ol_stride_head % 2 || out_stride_tok % 2 || out_stride_head % 2 ||
+      (reinterpret_cast<uintptr_t>(o_l) & 3) || (reinterpret_cast<uintptr_t>(out) & 3) ||
+      (reinterpret_cast<uintptr_t>(o_part) & 7))
+    return fail(FOLD_ERR_ALIGNMENT, "merge: rows must start on element pairs");
+  MergeParams p{};
+  p.o_l = static_cast<const __nv_bfloat16*>(o_l), p.ol_st = ol_stride_tok, p.ol_sh = ol_stride_head;
+  p.lse_l = lse_l, p.ll_sh = ll_stride_head, p.ll_st = ll_stride_tok;
+  p.o_f = o_part, p.of_bf16 = 0;
+  p.of_ss = static_cast<int64_t>(n) * hq * hd, p.of_st = static_cast<int64_t>(hq) * hd, p.of_sh = hd;
+  p.lse_f = lse_part, p.lf_ss = static_cast<int64_t>(hq) * n, p.lf_sh = n, p.lf_st = 1;
+  p.splits = splits;
+  p.out = static_cast<__nv_bfloat16*>(out), p.out_st = out_stride_tok, p.out_sh = out_stride_head;
+  p.qsl = qsl, p.seq = seq_lens, p.n = n, p.hq = hq, p.window = window, p.block = block, p.inv_alpha = inv_alpha;
+  return merge_launch(p, hd, false, stream);
+}
+
 }  // namespace fold
 
 extern "C" {

@@ -127,6 +127,27 @@ int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, c
 int fold_combine(const float* o_part, const float* lse_part, int splits, float* o_out, float* lse_out, int n, int hq,
                  int hd, void* stream);
 
+/* Far read + merge that allocates nothing, for callers that cannot allocate device memory when
+ * they run the draft step (an engine that plans every device buffer ahead of time and passes the
+ * attention plugin only the step's tensors, a C runtime without a caching allocator). No
+ * counterpart in the reference. The same work as fold_far_read followed by fold_merge, with the
+ * split partials kept in a 16 MiB static device array of the library (4 Mi floats per GPU, held
+ * from library load to process exit) instead of caller memory: requests needing more than
+ * splits * n * hq * (hd + 1) = 4194304 floats fail with FOLD_ERR_INVALID_ARGUMENT. The first call
+ * on each device looks the array up (cudaGetSymbolAddress); make it before any stream capture.
+ * The array is shared by every call on a device and keeps the last call's partials (each call
+ * overwrites all it reads), so calls that overlap on the GPU race: issue them on one stream.
+ * Arguments as fold_far_read (without qf and the partial buffers) and fold_merge (the window
+ * read o_l/lse_l and out). */
+int fold_far_read_merge_static(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                               const int* seq_lens, const float* rope_table, int table_rows, int rot_dim,
+                               const void* side, int pages, int64_t pos_lo, int64_t capacity, int* far_len,
+                               const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, const float* lse_l,
+                               int64_t ll_stride_head, int64_t ll_stride_tok, void* out, int64_t out_stride_tok,
+                               int64_t out_stride_head, int splits, int n, int hq, int hkv, int hd, int window,
+                               int block, int far_distance, float softmax_scale, float inv_alpha, int* err,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif
