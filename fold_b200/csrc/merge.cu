@@ -62,8 +62,11 @@ __device__ __forceinline__ void load_row(const void* base, int bf16, int64_t off
 }
 
 // Combines the far partials of (t, h) into acc (normalised) and returns their LSE (-inf if none).
+// Lane s holds split s's weight; the partial rows are loaded in batches of independent loads (the
+// partials sit in L2 right after the far read, so latency, not bandwidth, bounds this).
 template <int EPL>
 __device__ __forceinline__ float combine_far(const MergeParams& p, int t, int h, int lane, float (&acc)[EPL]) {
+  constexpr int BATCH = EPL <= 4 ? 16 : 8;
   const float* lf = p.lse_f + static_cast<int64_t>(h) * p.lf_sh + static_cast<int64_t>(t) * p.lf_st;
   float mx = -INFINITY;
   for (int s = lane; s < p.splits; s += 32) mx = fmaxf(mx, lf[s * p.lf_ss]);
@@ -73,16 +76,33 @@ __device__ __forceinline__ float combine_far(const MergeParams& p, int t, int h,
   if (mx == -INFINITY) return -INFINITY;
   float wsum = 0.f;
   const int64_t base = static_cast<int64_t>(t) * p.of_st + static_cast<int64_t>(h) * p.of_sh + lane * EPL;
-  for (int s = 0; s < p.splits; ++s) {
-    const float l = lf[s * p.lf_ss];
-    if (l == -INFINITY) continue;  // an empty split carries no mass
-    const float w = expf(l - mx);
+  for (int s0 = 0; s0 < p.splits; s0 += 32) {
+    const int cnt = min(32, p.splits - s0);
+    const float l = lane < cnt ? lf[(s0 + lane) * p.lf_ss] : -INFINITY;
+    const float w = l == -INFINITY ? 0.f : expf(l - mx);  // an empty split carries no mass
     wsum += w;
-    float v[EPL];
-    load_row<EPL>(p.o_f, p.of_bf16, base + s * p.of_ss, v);
+    for (int j = 0; j < cnt; j += BATCH) {
+      float v[BATCH][EPL];
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+      for (int u = 0; u < BATCH; ++u) {
+        if (j + u < cnt) {
+          load_row<EPL>(p.o_f, p.of_bf16, base + (s0 + j + u) * p.of_ss, v[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) v[u][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < BATCH; ++u) {
+        const float wu = __shfl_sync(0xffffffffu, w, (j + u) & 31);
+        if (j + u < cnt) {
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) acc[i] = fmaf(wu, v[u][i], acc[i]);
+        }
+      }
+    }
   }
+  wsum = warp_sum(wsum);
   const float inv = 1.f / wsum;
 #pragma unroll
   for (int i = 0; i < EPL; ++i) acc[i] *= inv;

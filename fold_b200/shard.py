@@ -47,7 +47,7 @@ class ShardPlan:
 
     @property
     def pos_lo(self) -> int:
-        return min(self.rank * self.chunk, self.length)
+        return self.rank * self.chunk  # a rank past the end holds nothing (held == 0)
 
     @property
     def held(self) -> int:

@@ -1,0 +1,106 @@
+"""The sharded far memory on 2 GPUs over NCCL with the CUDA kernels: each rank appends only its
+positions, reads its chunk, combines its splits and all-gathers; the merged output must match the
+unsharded far read + merge on one GPU. Skipped with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+    pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def inputs(device):
+    g = torch.Generator().manual_seed(5)
+    n, hq, hkv, hd, W = 10, 32, 8, 128, 512
+    length = 20000
+    hist = length - n
+    k = torch.randn((length, hkv, hd), generator=g).to(torch.bfloat16)
+    v = torch.randn((length, hkv, hd), generator=g).to(torch.bfloat16)
+    q = torch.randn((n, hq, hd), generator=g).to(torch.bfloat16)
+    o_l = torch.randn((n, hq, hd), generator=g).to(torch.bfloat16)
+    lse_l = torch.randn((hq, n), generator=g) + 4
+    return dict(n=n, hq=hq, hkv=hkv, hd=hd, W=W, length=length, hist=hist, k=k.to(device), v=v.to(device),
+                q=q.to(device), o_l=o_l.to(device), lse_l=lse_l.to(device))
+
+
+def step(p, ws, device, sharded=None):
+    from fold_b200 import kernels
+    pos = torch.arange(p["hist"], device=device)
+    ws.append(p["k"][: p["hist"]], p["v"][: p["hist"]], pos, pos)
+    qsl = torch.tensor([0, p["n"]], dtype=torch.int32, device=device)
+    seq = torch.tensor([p["length"]], dtype=torch.int32, device=device)
+    out = torch.empty((p["n"], p["hq"], p["hd"]), device=device, dtype=torch.bfloat16)
+    scale = p["hd"] ** -0.5
+    if sharded is None:
+        o_part, lse_part = ws.read_far(p["q"], qsl, seq, scale)
+        kernels.merge(p["o_l"], p["lse_l"], o_part, lse_part, out, qsl, seq, window=p["W"], block=p["n"], alpha=2.0)
+    else:
+        o_all, lse_all = sharded.step(p["q"], qsl, seq, scale)
+        sharded.merge(p["o_l"], p["lse_l"], o_all, lse_all, out, qsl, seq)
+    torch.cuda.synchronize(device)
+    ws.check()
+    return out.float().cpu()
+
+
+def workspace(p, device, plan=None):
+    from fold_b200.attention import FoldWorkspace
+    from fold_b200.rope import default_inv_freq
+    dummy = torch.zeros((1, p["hkv"], 16, 2 * p["hd"]), device=device, dtype=torch.bfloat16)
+    inv = default_inv_freq(500000.0, p["hd"], device)
+    if plan is None:
+        return FoldWorkspace(dummy, p["W"], p["n"], p["length"], inv_freq=inv, far_distance=p["W"] + p["n"],
+                             num_heads=p["hq"])
+    return plan.workspace(dummy, p["W"], p["n"], inv_freq=inv, far_distance=p["W"] + p["n"], num_heads=p["hq"])
+
+
+def worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from fold_b200.shard import ShardedFarMemory, ShardPlan
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    try:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=device)
+        p = inputs(device)
+        plan = ShardPlan.even(p["length"], world, rank)
+        ws = workspace(p, device, plan)
+        out = step(p, ws, device, ShardedFarMemory(plan, ws))
+        q.put((rank, "ok", out.numpy()))
+    except Exception as e:
+        q.put((rank, "error", repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_two_gpu_sharded_read_matches_single_gpu():
+    device = torch.device("cuda", 0)
+    p = inputs(device)
+    want = step(p, workspace(p, device), device).numpy()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=worker, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = dict((r, (s, x)) for r, s, x in (q.get(timeout=300) for _ in range(2)))
+    for pr in procs:
+        pr.join(timeout=60)
+    for r in (0, 1):
+        assert res[r][0] == "ok", res[r]
+        assert np.abs(res[r][1] - want).max() <= 2e-2
