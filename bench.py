@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0, help="far-read splits per KV head (0: one CTA per SM)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch the timed steps from Python, not as a CUDA graph")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     return ap.parse_args()
 
@@ -267,20 +268,18 @@ def run_gpu(args):
     o_mine, lse_mine = send[: B * hq * hd].view(B, hq, hd), send[B * hq * hd:].view(hq, B)
     scale = hd ** -0.5 * ALPHA
     stream = torch.cuda.current_stream(dev)
-    ev_far = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
-    def step(i, timed_idx=None):
+    def far(i):
+        kernels.far_read(q_all[i], qsl, seq_all[i: i + 1], side, o_part, lse_part, window=W, block=B,
+                         far_distance=W + B, softmax_scale=scale, table=table, pos_lo=pos_lo, capacity=length, err=err)
+
+    def step(i):
         a = int(acc[i - 1]) if i > 0 else 0
         if a:  # tokens accepted by the previous step become committed context
             kernels.append(new_k[i - 1, :a], new_v[i - 1, :a], new_pos[i - 1, :a], new_pos[i - 1, :a], side,
                            pos_lo=pos_lo, skip_foreign=world > 1, err=err)
         seq = seq_all[i: i + 1]
-        if timed_idx is not None:
-            ev_far[timed_idx][0].record(stream)
-        kernels.far_read(q_all[i], qsl, seq, side, o_part, lse_part, window=W, block=B, far_distance=W + B,
-                         softmax_scale=scale, table=table, pos_lo=pos_lo, capacity=length, err=err)
-        if timed_idx is not None:
-            ev_far[timed_idx][1].record(stream)
+        far(i)
         if world > 1:
             kernels.combine(o_part, lse_part, o_mine, lse_mine)
             dist.all_gather_into_tensor(recv, send)
@@ -296,19 +295,54 @@ def run_gpu(args):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    # The K timed steps run as one CUDA graph (the drafter step runs inside vLLM's CUDA graphs);
+    # --eager launches them one by one from Python instead.
+    graph = None
+    if not args.eager:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for j in range(args.steps):
+                step(args.warmup + j)
+        torch.cuda.synchronize()
+
+    def timed_steps():
+        if graph is not None:
+            graph.replay()
+        else:
+            for j in range(args.steps):
+                step(args.warmup + j)
+
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        # clocks are sampled over a short untimed soak of the same steps and the timed region
+        t_soak = time.perf_counter()
+        while graph is not None and time.perf_counter() - t_soak < 0.6:
+            graph.replay()
+            torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
         e0.record(stream)
-        for j in range(args.steps):
-            step(args.warmup + j, j)
+        timed_steps()
         e1.record(stream)
         torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    far_ms = sum(a.elapsed_time(b) for a, b in ev_far) / args.steps
+    # The far-read kernel alone (roofline): the same K launches back to back, timed with events
+    # around one replay of a graph that holds only them.
+    far_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(far_graph):
+        for j in range(args.steps):
+            far(args.warmup + j)
+    far_graph.replay()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    far_graph.replay()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    far_ms = f0.elapsed_time(f1) / args.steps
+    del far_graph
     if int(err.item()):
         raise RuntimeError(f"device error word {int(err.item())}")
     t = torch.tensor([ms, far_ms], device=dev, dtype=torch.float64)
@@ -347,6 +381,7 @@ def run_gpu(args):
             "config": {"workload": cfg["name"], "context": cfg["ctx"], "window": W, "block": B, "heads_q": hq,
                        "heads_kv": hkv, "head_dim": hd, "alpha": ALPHA, "splits": splits,
                        "parallelism": f"seq-shard{world}" if world > 1 else "single",
+                       "timing": "eager launches" if args.eager else "CUDA graph of the K timed steps",
                        "l2": "inputs larger than L2 (side cache %.0f MB per GPU)" % (side.numel() * 2 / 1e6)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
@@ -359,6 +394,7 @@ def run_gpu(args):
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, args.seed)
         print(json.dumps(line), flush=True)
+    del graph
     if world > 1:
         dist.destroy_process_group()
 

@@ -9,9 +9,11 @@
 //   O^T += V^T . P^T
 // on bf16 mma.sync tiles, and finally write the split's normalised partial (o, lse).
 //
-// The running row maximum m only moves when a new logit exceeds it by more than 2^kRaise, which
-// is decided for the whole CTA by one OR-barrier per tile. So the common tile needs no cross-warp
-// max exchange and no rescaling; P stays below 2^kRaise (exact in fp32, fine in bf16).
+// The running row maximum m only moves when a new logit exceeds it by more than kRaise (log2
+// units), which is decided for the whole CTA by one OR-barrier per tile. So the common tile needs
+// no cross-warp max exchange and no rescaling. P stays below 2^kRaise: bf16 keeps its 8-bit
+// mantissa at any magnitude and the fp32 sums of at most 2^16 * (keys per split) stay far from
+// overflow, so a high threshold costs no accuracy and makes raises rare after the first tile.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -22,7 +24,7 @@
 
 namespace fold {
 
-constexpr float kRaise = 8.0f;
+constexpr float kRaise = 16.0f;
 
 struct FarParams {
   const __nv_bfloat16* q;
@@ -41,6 +43,7 @@ struct FarParams {
   int window, block, far_distance;
   float scale_log2;
   int* err;
+  int vec_rot;  // q, qf and the table rows allow the 16-byte vector path of the rotation
 };
 
 constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100
@@ -101,6 +104,81 @@ __device__ __forceinline__ void issue_tile(unsigned char* smem, uint64_t* full, 
   for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
 }
 
+// Vectorised far-query rotation: each work item is one row's pair of 8-element chunks
+// ([8c, 8c+8) with its neox partner [RH+8c, ...), or 16 unrotated elements), loaded as 16-byte
+// vectors. Every thread issues the loads of all its items before any arithmetic, so the prologue
+// costs one memory latency instead of one per element.
+template <class C>
+__device__ __forceinline__ void rotate_query_vec(const FarParams& p, const float* trow, int RH, float sgn, int h,
+                                                 int split, int nrows, int G, __nv_bfloat16* Qs) {
+  constexpr int PAIRS = C::HD / 16;
+  constexpr int ITEMS = C::ROWS * PAIRS;
+  constexpr int MAXI = (ITEMS + C::NTHREADS - 1) / C::NTHREADS;
+  const int tid = threadIdx.x;
+  const int rh8 = trow ? RH / 8 : 0;
+  uint4 qa[MAXI], qb[MAXI];
+  float4 c0[MAXI], c1[MAXI], s0[MAXI], s1[MAXI];
+#pragma unroll
+  for (int k = 0; k < MAXI; ++k) {
+    const int e = tid + k * C::NTHREADS;
+    qa[k] = qb[k] = make_uint4(0, 0, 0, 0);
+    c0[k] = c1[k] = s0[k] = s1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < ITEMS) {
+      const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
+      if (rho < nrows) {
+        const int r = rho / G, hq = h * G + (rho - r * G);
+        const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
+        if (c < rh8) {
+          qa[k] = __ldg(reinterpret_cast<const uint4*>(qr + 8 * c));
+          qb[k] = __ldg(reinterpret_cast<const uint4*>(qr + RH + 8 * c));
+          const float4* tc = reinterpret_cast<const float4*>(trow + 8 * c);
+          const float4* ts = reinterpret_cast<const float4*>(trow + RH + 8 * c);
+          c0[k] = __ldg(tc), c1[k] = __ldg(tc + 1), s0[k] = __ldg(ts), s1[k] = __ldg(ts + 1);
+        } else {
+          const int off = 2 * RH * (rh8 > 0) + 16 * (c - rh8);
+          qa[k] = __ldg(reinterpret_cast<const uint4*>(qr + off));
+          qb[k] = __ldg(reinterpret_cast<const uint4*>(qr + off + 8));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < MAXI; ++k) {
+    const int e = tid + k * C::NTHREADS;
+    if (e >= ITEMS) continue;
+    const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
+    int off_a, off_b;
+    uint4 ya = qa[k], yb = qb[k];
+    if (c < rh8) {
+      off_a = 8 * c, off_b = RH + 8 * c;
+      const float cs[8] = {c0[k].x, c0[k].y, c0[k].z, c0[k].w, c1[k].x, c1[k].y, c1[k].z, c1[k].w};
+      const float sn[8] = {s0[k].x, s0[k].y, s0[k].z, s0[k].w, s1[k].x, s1[k].y, s1[k].z, s1[k].w};
+      const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&qa[k]);
+      const __nv_bfloat162* xb = reinterpret_cast<const __nv_bfloat162*>(&qb[k]);
+      uint32_t* oa = reinterpret_cast<uint32_t*>(&ya);
+      uint32_t* ob = reinterpret_cast<uint32_t*>(&yb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = __bfloat1622float2(xa[j]), xp = __bfloat1622float2(xb[j]);
+        const float c_0 = cs[2 * j], c_1 = cs[2 * j + 1];
+        const float s_0 = sgn * sn[2 * j], s_1 = sgn * sn[2 * j + 1];
+        oa[j] = pack_bf16(x.x * c_0 - xp.x * s_0, x.y * c_1 - xp.y * s_1);
+        ob[j] = pack_bf16(xp.x * c_0 + x.x * s_0, xp.y * c_1 + x.y * s_1);
+      }
+    } else {
+      off_a = 2 * RH * (rh8 > 0) + 16 * (c - rh8), off_b = off_a + 8;
+    }
+    *reinterpret_cast<uint4*>(Qs + rho * C::QSTRIDE + off_a) = ya;
+    *reinterpret_cast<uint4*>(Qs + rho * C::QSTRIDE + off_b) = yb;
+    if (p.qf && split == 0 && rho < nrows) {
+      const int r = rho / G, hq = h * G + (rho - r * G);
+      __nv_bfloat16* o = p.qf + r * p.qf_st + hq * p.qf_sh;
+      *reinterpret_cast<uint4*>(o + off_a) = ya;
+      *reinterpret_cast<uint4*>(o + off_b) = yb;
+    }
+  }
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
@@ -158,27 +236,31 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     }
     const int RH = p.rot_dim >> 1;
     const float* trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
-    for (int e = tid; e < ROWS * HD; e += NTH) {
-      const int rho = e / HD, d = e - (e / HD) * HD;
-      float y = 0.f;
-      if (rho < nrows) {
-        const int r = rho / G, hq = h * G + (rho - r * G);
-        const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
-        const float x = bf2f(qr[d]);
-        if (trow && d < 2 * RH) {
-          const bool lo = d < RH;
-          const int i = lo ? d : d - RH;
-          const float xp = bf2f(qr[lo ? d + RH : d - RH]);
-          const float c = trow[i], s = sgn * trow[RH + i];
-          y = lo ? x * c - xp * s : x * c + xp * s;
+    if (p.vec_rot) {
+      rotate_query_vec<C>(p, trow, RH, sgn, h, split, nrows, G, Qs);
+    } else {
+      for (int e = tid; e < ROWS * HD; e += NTH) {
+        const int rho = e / HD, d = e - (e / HD) * HD;
+        float y = 0.f;
+        if (rho < nrows) {
+          const int r = rho / G, hq = h * G + (rho - r * G);
+          const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
+          const float x = bf2f(qr[d]);
+          if (trow && d < 2 * RH) {
+            const bool lo = d < RH;
+            const int i = lo ? d : d - RH;
+            const float xp = bf2f(qr[lo ? d + RH : d - RH]);
+            const float c = trow[i], s = sgn * trow[RH + i];
+            y = lo ? x * c - xp * s : x * c + xp * s;
+          } else {
+            y = x;
+          }
+          const __nv_bfloat16 yb = __float2bfloat16_rn(y);
+          if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
+          Qs[rho * C::QSTRIDE + d] = yb;
         } else {
-          y = x;
+          Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);
         }
-        const __nv_bfloat16 yb = __float2bfloat16_rn(y);
-        if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
-        Qs[rho * C::QSTRIDE + d] = yb;
-      } else {
-        Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);
       }
     }
   }
@@ -286,19 +368,24 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
           exceed |= v > MQ(j, c) + kRaise;
         }
       }
+      if (it == 0) {
+        exceed = true;  // the first tile always sets the row maxima: skip the provisional P
+      } else {
 #pragma unroll
-      for (int j = 0; j < QNT; ++j) {
-        const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
-        const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
-        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
-        ls[j][0] = p0 + p2;
-        ls[j][1] = p1 + p3;
-        if (nt_lo + j < NT) {
-          const int r0 = (nt_lo + j) * 8 + t4 * 2;
-          const int k0 = mt * 16 + g4;
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p2, p3)));
+        for (int j = 0; j < QNT; ++j) {
+          const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
+          const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
+          const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+          const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+          ls[j][0] = p0 + p2;
+          ls[j][1] = p1 + p3;
+          if (nt_lo + j < NT) {
+            const int r0 = (nt_lo + j) * 8 + t4 * 2;
+            const int k0 = mt * 16 + g4;
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2),
+                         "r"(pack_bf16(p2, p3)));
+          }
         }
       }
     }
@@ -490,6 +577,18 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
 }
 
 // ------------------------------------------------------------------ host side
+// Whether the 16-byte vector rotation applies: 16-byte aligned rows of q (and qf), rotary halves
+// in whole 8-element chunks, unrotated tail in whole 16-element pairs.
+static int vec_rotation_ok(const void* q, int64_t q_st, int64_t q_sh, const void* qf, int64_t qf_st, int64_t qf_sh,
+                           const float* table, int rot_dim, int hd) {
+  if (!aligned16(q) || q_st % 8 || q_sh % 8) return 0;
+  if (qf && (!aligned16(qf) || qf_st % 8 || qf_sh % 8)) return 0;
+  if (table) {
+    if (!aligned16(table) || rot_dim % 16 || (hd - rot_dim) % 16) return 0;
+  }
+  return 1;
+}
+
 template <class C>
 int launch_far(const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
   CUtensorMap map;
@@ -583,6 +682,7 @@ int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   prm.window = window, prm.block = block, prm.far_distance = far_distance;
   prm.scale_log2 = softmax_scale * kLog2e;
   prm.err = err;
+  prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, nullptr, 0, 0, rope_table, rot_dim, hd);
   const int nt = (rows + 7) / 8;
   if (hd == 128) return dispatch_nt_uncached<128, 128, 4>(nt, prm, side, pages, stream);
   return dispatch_nt_uncached<256, 64, 8>(nt, prm, side, pages, stream);
@@ -632,6 +732,7 @@ int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, co
   prm.window = window, prm.block = block, prm.far_distance = far_distance;
   prm.scale_log2 = softmax_scale * kLog2e;
   prm.err = err;
+  prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, qf, qf_stride_tok, qf_stride_head, rope_table, rot_dim, hd);
   const int nt = (rows + 7) / 8;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (hd == 128) return dispatch_nt<128, 128, 4>(nt, prm, side, pages, s);
