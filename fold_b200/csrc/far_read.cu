@@ -17,36 +17,16 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
+#include "far_read.cuh"
 #include "host_common.h"
 
 namespace fold {
-
-constexpr float kRaise = 16.0f;
-
-struct FarParams {
-  const __nv_bfloat16* q;
-  int64_t q_st, q_sh;
-  const int* qsl;
-  const int* seq;
-  const float* table;
-  int table_rows, rot_dim;
-  int64_t pos_lo, capacity, local_cap;
-  int* far_len;
-  __nv_bfloat16* qf;
-  int64_t qf_st, qf_sh;
-  float* o_part;
-  float* lse_part;
-  int splits, n, hq, hkv, group;
-  int window, block, far_distance;
-  float scale_log2;
-  int* err;
-  int vec_rot;  // q, qf and the table rows allow the 16-byte vector path of the rotation
-};
-
-constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100
 
 template <int HD_, int NT_, int TK_, int HG_>
 struct FarCfg {
@@ -87,9 +67,6 @@ struct FarCfg {
   static_assert(TK <= 256 && 256 % TK == 0, "tiles stay inside one 256-entry page");
 };
 
-__device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
-__device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
-__device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 // Issues the TMA copies of tile `tile` (index in this cache) of head h into stage `st`.
 template <class C>
@@ -577,6 +554,28 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
 }
 
 // ------------------------------------------------------------------ host side
+namespace {
+// -2: not read yet; -1: choose per shape; 0: mma.sync; 1: tcgen05.
+std::atomic<int> g_far_variant{-2};
+}  // namespace
+
+int far_read_variant(int hd, int rows) {
+  int v = g_far_variant.load(std::memory_order_relaxed);
+  if (v == -2) {
+    const char* e = getenv("FOLD_FAR_READ_KERNEL");
+    v = (e && !strcmp(e, "mma")) ? 0 : (e && !strcmp(e, "tc")) ? 1 : -1;
+    int expected = -2;
+    g_far_variant.compare_exchange_strong(expected, v);
+    v = g_far_variant.load(std::memory_order_relaxed);
+  }
+  if (v >= 0) return v;
+  // The mma.sync kernel streams at HBM speed while its tensor work fits; past 48 query rows per
+  // KV head it becomes tensor-bound and the tcgen05 kernel is faster.
+  (void)hd;
+  return rows > 48 ? 1 : 0;
+}
+
+
 // Whether the 16-byte vector rotation applies: 16-byte aligned rows of q (and qf), rotary halves
 // in whole 8-element chunks, unrotated tail in whole 16-element pairs.
 static int vec_rotation_ok(const void* q, int64_t q_st, int64_t q_sh, const void* qf, int64_t qf_st, int64_t qf_sh,
@@ -684,6 +683,8 @@ int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   prm.err = err;
   prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, nullptr, 0, 0, rope_table, rot_dim, hd);
   const int nt = (rows + 7) / 8;
+  if (far_read_variant(hd, rows) == 1)
+    return far_read_tc_launch(prm, side, pages, hd, ((rows + 15) / 16) * 16, false, stream);
   if (hd == 128) return dispatch_nt_uncached<128, 128, 4>(nt, prm, side, pages, stream);
   return dispatch_nt_uncached<256, 64, 8>(nt, prm, side, pages, stream);
 }
@@ -691,6 +692,12 @@ int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head
 }  // namespace fold
 
 extern "C" {
+
+int fold_far_read_select_kernel(int kernel) {
+  if (kernel < -1 || kernel > 1) return fold::fail(FOLD_ERR_INVALID_ARGUMENT, "far read kernel: -1, 0 or 1");
+  fold::g_far_variant.store(kernel);
+  return FOLD_OK;
+}
 
 int fold_far_read_default_splits(int hkv, int hd, int n, int hq) {
   (void)hd, (void)n, (void)hq;
@@ -735,6 +742,7 @@ int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, co
   prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, qf, qf_stride_tok, qf_stride_head, rope_table, rot_dim, hd);
   const int nt = (rows + 7) / 8;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (far_read_variant(hd, rows) == 1) return far_read_tc_launch(prm, side, pages, hd, ((rows + 15) / 16) * 16, true, s);
   if (hd == 128) return dispatch_nt<128, 128, 4>(nt, prm, side, pages, s);
   return dispatch_nt<256, 64, 8>(nt, prm, side, pages, s);
 }

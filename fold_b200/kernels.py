@@ -189,6 +189,17 @@ def combine(o_part, lse_part, o_out=None, lse_out=None):
     return o_out, lse_out
 
 
+FAR_READ_KERNELS = {"auto": -1, "mma": 0, "tc": 1}
+
+
+def select_far_read_kernel(kernel: str = "auto") -> None:
+    """Choose the far-read kernel for later calls: "mma" (mma.sync tiles), "tc" (tcgen05 tiles with
+    TMEM accumulators) or "auto" (per shape)."""
+    if kernel not in FAR_READ_KERNELS:
+        raise FoldError(f"far-read kernel must be one of {sorted(FAR_READ_KERNELS)}")
+    _lib.call("fold_far_read_select_kernel", FAR_READ_KERNELS[kernel])
+
+
 def default_splits(hkv):
     """Split count per KV head that fills the device with one CTA per SM."""
     return _lib.default_splits(hkv, 0, 0, 0)

@@ -103,6 +103,12 @@ int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, co
                   float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd, int window, int block,
                   int far_distance, float softmax_scale, int* err, void* stream);
 
+/* Chooses the far-read kernel for later calls: 0 = mma.sync tiles, 1 = tcgen05 tiles with TMEM
+ * accumulators, -1 = per shape (the default: tcgen05 above 48 query rows per KV head). Both give
+ * the same results within rounding. The environment variable FOLD_FAR_READ_KERNEL=mma|tc sets
+ * the initial choice. No reference counterpart (a tuning switch of this implementation). */
+int fold_far_read_select_kernel(int kernel);
+
 /* Split count that fills the device for `hkv` KV heads (one CTA per SM). */
 int fold_far_read_default_splits(int hkv, int hd, int n, int hq);
 

@@ -52,3 +52,13 @@ def test_argument_errors_are_reported_without_a_gpu():
                   1, 1, 128, 1, 1, 0.5, None)
     # an empty append is a no-op that needs no device
     _lib.call("fold_append", None, 0, 0, None, 0, 0, None, None, 0, None, 2, 1, 128, 0, 0, None, None)
+
+
+def test_kernel_selection_validates():
+    from fold_b200 import kernels
+    with pytest.raises(FoldError):
+        kernels.select_far_read_kernel("fastest")
+    with pytest.raises(FoldError, match="far read kernel"):
+        _lib.call("fold_far_read_select_kernel", 7)
+    kernels.select_far_read_kernel("tc")
+    kernels.select_far_read_kernel("auto")

@@ -53,7 +53,7 @@ CASES = golden_block_names(min_hd=128)
 
 
 @pytest.mark.parametrize("name", CASES)
-def test_fold_forward_matches_reference(name):
+def test_fold_forward_matches_reference(name, far_kernel):
     g = golden_block_case(name)
     ws, original, meta, query, kv_cache, output = build_step(g)
     layer = FoldAttention(original, ws, local_read=torch_local_read)

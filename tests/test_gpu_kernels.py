@@ -179,31 +179,31 @@ FAR_CASES = [
 
 
 @pytest.mark.parametrize("n,hq,hkv,hd,far_keys,splits", FAR_CASES)
-def test_far_read_matches_oracle(n, hq, hkv, hd, far_keys, splits):
+def test_far_read_matches_oracle(n, hq, hkv, hd, far_keys, splits, far_kernel):
     o_d, lse_d, o_w, lse_w, x = run_far(n, hq, hkv, hd, far_keys, splits=splits, extra=300, seed=far_keys)
     assert np.abs(o_d - o_w).max() <= OUT_ATOL
     lse_close(lse_d, lse_w)
 
 
-def test_far_read_no_far_keys_gives_empty_rows():
+def test_far_read_no_far_keys_gives_empty_rows(far_kernel):
     o_d, lse_d, o_w, lse_w, _ = run_far(10, 32, 8, 128, 0, splits=4, extra=50)
     assert np.all(np.isneginf(lse_d)) and np.all(o_d == 0)
 
 
-def test_far_read_outliers_partial_rotary():
+def test_far_read_outliers_partial_rotary(far_kernel):
     o_d, lse_d, o_w, lse_w, x = run_far(10, 32, 8, 128, 3000, splits=8, outliers=4, rot=64, extra=200)
     out_close(o_d, o_w, x["vscale"])
     lse_close(lse_d, lse_w)
 
 
-def test_far_read_shard_of_cache():
+def test_far_read_shard_of_cache(far_kernel):
     """A shard holding positions [512, 1536) of a 4000-key far memory."""
     o_d, lse_d, o_w, lse_w, _ = run_far(10, 32, 8, 128, 4000, splits=6, pos_lo=512, held=1024, extra=0)
     assert np.abs(o_d - o_w).max() <= OUT_ATOL
     lse_close(lse_d, lse_w)
 
 
-def test_far_read_full_context_llama_shape():
+def test_far_read_full_context_llama_shape(far_kernel):
     """Llama-3.1-8B drafter shape at 131072 context (129024 far keys), outlier channels x8."""
     o_d, lse_d, o_w, lse_w, x = run_far(10, 32, 8, 128, 129024, splits=18, window=2048, outliers=4, seed=1)
     out_close(o_d, o_w, x["vscale"])
