@@ -121,6 +121,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Arrives on named barrier `id` (expecting `nthreads` in total) without waiting.
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 // Barrier over `nthreads` threads that also returns the OR of `pred` across them.
 __device__ __forceinline__ bool named_bar_or(bool pred, int id, int nthreads) {
   uint32_t out;

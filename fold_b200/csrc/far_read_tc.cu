@@ -68,6 +68,62 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// N (16..64, multiple of 16) consecutive columns with one wait for all of them.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
+  static_assert(N % 16 == 0 && N <= 64, "columns");
+  uint32_t r[64];
+  if constexpr (N == 16) {
+    tmem_ld16(taddr, v);
+    return;
+  } else if constexpr (N == 32) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+  } else if constexpr (N == 48) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%48];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47},"
+        " [%49];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
+        : "r"(taddr), "r"(taddr + 32)
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
@@ -95,6 +151,31 @@ constexpr uint32_t idesc_bf16(int m, int n, int a_mn, int b_mn) {
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Position in the TMA load sequence of unit j (j < KU: K unit, else V unit j-KU) of tile t. The
+// sequence is K(0), then per tile b: K(b+1) (when it exists) and V(b), i.e. the order in which the
+// MMAs consume them, so a V unit does not sit landed while the softmax of its tile runs.
+__device__ __forceinline__ int unit_seq(int t, int j, int ntiles, int KU) {
+  const int UPT = 2 * KU;
+  if (j < KU) return t == 0 ? j : KU + (t - 1) * UPT + j;
+  const int r = j - KU;
+  return t + 1 < ntiles ? KU + t * UPT + KU + r : KU + t * UPT + r;
+}
+// Inverse: tile and unit index of sequence position q.
+__device__ __forceinline__ void unit_of(int q, int ntiles, int KU, int& t, int& j) {
+  const int UPT = 2 * KU;
+  if (q < KU) {
+    t = 0, j = q;
+    return;
+  }
+  const int qq = q - KU, b = qq / UPT, r = qq - (qq / UPT) * UPT;
+  if (b + 1 < ntiles) {
+    if (r < KU) t = b + 1, j = r;
+    else t = b, j = r;  // V unit r - KU of tile b
+  } else {
+    t = b, j = KU + r;
+  }
+}
+
 template <int HD_, int NP_>
 struct TcCfg {
   static constexpr int HD = HD_, NP = NP_, TK = 128;
@@ -111,12 +192,16 @@ struct TcCfg {
   static constexpr int RED_BYTES = NSW * NP * 4;
   static constexpr int ROW_BYTES = 3 * NP * 4;  // row limits, row maxima, rescale factors
   static constexpr int NBAR = 26;
-  static constexpr int FIXED = Q_BYTES + 2 * P_BYTES + RED_BYTES + ROW_BYTES + NBAR * 8 + 16 + 1024;
-  static constexpr int NSLOT_FIT = (kSmemLimit - FIXED) / UNIT_BYTES;
+  static constexpr int BASE_FIXED = Q_BYTES + RED_BYTES + ROW_BYTES + NBAR * 8 + 16 + 1024;
+  static constexpr int fit(int pbufs) { return (kSmemLimit - BASE_FIXED - pbufs * P_BYTES) / UNIT_BYTES; }
+  // Two P^T buffers let the softmax of tile i+1 write while the PV MMAs of tile i read; one buffer
+  // is used when it buys another ring slot (more K/V bytes in flight matter more).
+  static constexpr int P_BUFS = fit(1) > fit(2) ? 1 : 2;
+  static constexpr int NSLOT_FIT = fit(P_BUFS);
   static constexpr int NSLOT = NSLOT_FIT > 8 ? 8 : NSLOT_FIT;
   static constexpr int OFF_Q = NSLOT * UNIT_BYTES;
   static constexpr int OFF_P = OFF_Q + Q_BYTES;
-  static constexpr int OFF_RED = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_RED = OFF_P + P_BUFS * P_BYTES;
   static constexpr int OFF_ROW = OFF_RED + RED_BYTES;
   static constexpr int OFF_BAR = OFF_ROW + ROW_BYTES;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
@@ -253,7 +338,6 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   uint64_t* s_free = bars + 18;  // [2] S^T buffer read by the softmax warps
   uint64_t* p_full = bars + 20;  // [2] P^T written (and O^T rescaled) for the tile
   uint64_t* pv_done = bars + 22; // [2] the PV MMAs of the tile completed
-  uint64_t* q_ready = bars + 24;
   uint64_t* o_final = bars + 25;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_TMEM);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
@@ -276,34 +360,59 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / p.splits);
   const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / p.splits) - t_begin;
 
-  if (tid == 0) {
-    if (split == 0 && h == 0) {
-      if (p.far_len) *p.far_len = far_len;
-      if (far_len > p.capacity) set_error(p.err, FOLD_DEVERR_CAPACITY);
+  // Prologue. The producer warp initialises the mbarriers and starts streaming at once (named
+  // barrier 3 releases the other warps once the barriers exist); warp 0 allocates TMEM; the
+  // softmax warps rotate the query meanwhile. Named barrier 4 (softmax + MMA warps) then publishes
+  // the TMEM address and the finished query tile.
+  if (warp == C::NSW) {
+    if (lane == 0) {
+      if (split == 0 && h == 0) {
+        if (p.far_len) *p.far_len = far_len;
+        if (far_len > p.capacity) set_error(p.err, FOLD_DEVERR_CAPACITY);
+      }
+      for (int i = 0; i < NSLOT; ++i) mbar_init(&full[i], 1), mbar_init(&empty[i], 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&s_full[b], 1);
+        mbar_init(&s_free[b], C::NSW);
+        mbar_init(&p_full[b], C::NSW);
+        mbar_init(&pv_done[b], 1);
+      }
+      mbar_init(o_final, 1);
+      fence_mbar_init();
     }
-    for (int i = 0; i < NSLOT; ++i) mbar_init(&full[i], 1), mbar_init(&empty[i], 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], C::NSW);
-      mbar_init(&p_full[b], C::NSW);
-      mbar_init(&pv_done[b], 1);
+    __syncwarp();
+    named_bar_arrive(3, C::NTHREADS);
+  } else {
+    if (warp == 0) {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
     }
-    mbar_init(q_ready, 1);
-    mbar_init(o_final, 1);
-    fence_mbar_init();
+    if (warp < C::NSW) {
+      if (tid < NP) {
+        lims[tid] = tid < nrows ? static_cast<int>(min64(lim_base + tid / G, end)) : 0;
+        rowm[tid] = -INFINITY;
+      }
+      const int delta = p.far_distance - hist;
+      int ad = delta < 0 ? -delta : delta;
+      const float sgn = delta < 0 ? -1.f : 1.f;
+      if (p.table && ad >= p.table_rows) {
+        if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
+        ad = p.table_rows - 1;
+      }
+      const int RH = p.rot_dim >> 1;
+      const float* trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
+      if (p.vec_rot)
+        rotate_query_tc<C>(p, trow, RH, sgn, h, split, nrows, G, smem + C::OFF_Q);
+      else
+        rotate_query_tc_scalar<C>(p, trow, RH, sgn, h, split, nrows, G, smem + C::OFF_Q);
+      fence_proxy_async();  // Q is read by the tensor cores
+    }
+    named_bar_sync(3, C::NTHREADS);  // the mbarriers exist
+    tc_fence_before();
+    named_bar_sync(4, C::NSM + 32);  // TMEM address, row limits and Q are ready
+    tc_fence_after();
   }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
-  }
-  if (tid < NP) {
-    lims[tid] = tid < nrows ? static_cast<int>(min64(lim_base + tid / G, end)) : 0;
-    rowm[tid] = -INFINITY;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = warp == C::NSW ? 0u : *tmem_slot;  // the producer never touches TMEM
 
   if (warp == C::NSW) {
     // -------------------------------------------------------------- TMA producer
@@ -319,9 +428,11 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[slot], C::UNIT_BYTES);
-        const int64_t lp = static_cast<int64_t>(t_begin + u / UPT) * TK;  // key index in this cache
+        int ut, uj;
+        unit_of(u, ntiles, KU, ut, uj);
+        const int64_t lp = static_cast<int64_t>(t_begin + ut) * TK;  // key index in this cache
         const int page = static_cast<int>(lp >> 8), off = static_cast<int>(lp & 255);
-        const int c2 = page * p.hkv + h, col = (u % UPT) * 128;
+        const int c2 = page * p.hkv + h, col = uj * 128;
         unsigned char* dst = smem + slot * C::UNIT_BYTES;
         tma_load_3d(dst, &map, &full[slot], col, off, c2, pol);
         tma_load_3d(dst + C::BOX_BYTES, &map, &full[slot], col + 64, off, c2, pol);
@@ -334,8 +445,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   } else if (warp == C::NSW + 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0 && ntiles > 0) {
-      bool ok = mbar_wait(q_ready, 0);
-      tc_fence_after();
+      bool ok = true;
       constexpr uint32_t idesc_s = idesc_bf16(128, NP, 0, 0);
       constexpr uint32_t idesc_o = idesc_bf16(128, NP, 1, 1);
       const uint32_t q_base = smem_u32(smem + C::OFF_Q);
@@ -346,7 +456,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
           const int b = i & 1;
           if (i >= 2) ok = mbar_wait(&s_free[b], ((i >> 1) - 1) & 1);
           for (int j = 0; ok && j < KU; ++j) {
-            const int u = i * UPT + j;
+            const int u = unit_seq(i, j, ntiles, KU);
             ok = mbar_wait(&full[u % NSLOT], (u / NSLOT) & 1);
           }
           if (!ok) break;
@@ -354,36 +464,36 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
           const uint32_t d = tmem + C::TMEM_S + b * NP;
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
-            const int u = i * UPT + (kk >> 3);
+            const int u = unit_seq(i, kk >> 3, ntiles, KU);
             const uint32_t a = slot_base + (u % NSLOT) * C::UNIT_BYTES + ((kk & 7) >> 2) * C::BOX_BYTES + (kk & 3) * 32;
             const uint32_t bq = q_base + (kk >> 2) * C::Q_CHUNK + (kk & 3) * 32;
             tc_mma(d, smem_desc(a, 16, 1024, kSwizzle128), smem_desc(bq, 16, 1024, kSwizzle128), idesc_s, kk > 0);
           }
           tc_commit(&s_full[b]);
-          for (int j = 0; j < KU; ++j) tc_commit(&empty[(i * UPT + j) % NSLOT]);
+          for (int j = 0; j < KU; ++j) tc_commit(&empty[unit_seq(i, j, ntiles, KU) % NSLOT]);
         }
         if (i >= 1) {
           const int t = i - 1, b = t & 1;
           ok = mbar_wait(&p_full[b], (t >> 1) & 1);
           for (int j = KU; ok && j < UPT; ++j) {
-            const int u = t * UPT + j;
+            const int u = unit_seq(t, j, ntiles, KU);
             ok = mbar_wait(&full[u % NSLOT], (u / NSLOT) & 1);
           }
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
           for (int hh = 0; hh < KU; ++hh) {
-            const int u = t * UPT + KU + hh;
+            const int u = unit_seq(t, KU + hh, ntiles, KU);
             const uint32_t v = slot_base + (u % NSLOT) * C::UNIT_BYTES;
 #pragma unroll
             for (int ks = 0; ks < TK / 16; ++ks) {
               tc_mma(tmem + C::TMEM_O + hh * NP, smem_desc(v + ks * 2048, C::BOX_BYTES, 1024, kSwizzle128),
-                     smem_desc(p_base + b * C::P_BYTES + ks * 256, 128, TK * 16, kSwizzleNone), idesc_o,
-                     (t > 0 || ks > 0));
+                     smem_desc(p_base + (t % C::P_BUFS) * C::P_BYTES + ks * 256, 128, TK * 16, kSwizzleNone),
+                     idesc_o, (t > 0 || ks > 0));
             }
           }
           tc_commit(&pv_done[b]);
-          for (int hh = 0; hh < KU; ++hh) tc_commit(&empty[(t * UPT + KU + hh) % NSLOT]);
+          for (int hh = 0; hh < KU; ++hh) tc_commit(&empty[unit_seq(t, KU + hh, ntiles, KU) % NSLOT]);
         }
       }
       if (!ok) set_error(p.err, FOLD_DEVERR_TIMEOUT);
@@ -392,25 +502,6 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     __syncwarp();
   } else {
     // -------------------------------------------------------------- softmax warps
-    {
-      const int delta = p.far_distance - hist;
-      int ad = delta < 0 ? -delta : delta;
-      const float sgn = delta < 0 ? -1.f : 1.f;
-      if (p.table && ad >= p.table_rows) {
-        if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
-        ad = p.table_rows - 1;
-      }
-      const int RH = p.rot_dim >> 1;
-      const float* trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
-      if (p.vec_rot)
-        rotate_query_tc<C>(p, trow, RH, sgn, h, split, nrows, G, smem + C::OFF_Q);
-      else
-        rotate_query_tc_scalar<C>(p, trow, RH, sgn, h, split, nrows, G, smem + C::OFF_Q);
-    }
-    fence_proxy_async();  // Q is read by the tensor cores
-    named_bar_sync(1, NSM);
-    if (tid == 0) mbar_arrive(q_ready);
-
     float l[NP];  // this thread's share of the row sums
 #pragma unroll
     for (int c = 0; c < NP; ++c) l[c] = 0.f;
@@ -427,8 +518,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
       float x[NP];
       if (ok) {
         tc_fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < NP; c0 += 16) tmem_ld16(tmem + C::TMEM_S + b * NP + c0 + lane_addr, &x[c0]);
+        tmem_ld_cols<NP>(tmem + C::TMEM_S + b * NP + lane_addr, x);
       } else {
 #pragma unroll
         for (int c = 0; c < NP; ++c) x[c] = -INFINITY;
@@ -492,8 +582,11 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
         }
       }
       // ---- P^T of this thread's key: 16-byte stores into [row group][key][8 rows]
-      if (i >= 2 && !mbar_wait(&pv_done[b], ((i - 2) >> 1) & 1)) bad = true;  // the PV MMAs of tile i-2 read it
-      unsigned char* pb = smem + p_base_gen + b * C::P_BYTES + tid * 16;
+      if (i >= C::P_BUFS) {  // the PV MMAs of tile i - P_BUFS read this buffer
+        const int t = i - C::P_BUFS;
+        if (!mbar_wait(&pv_done[t & 1], (t >> 1) & 1)) bad = true;
+      }
+      unsigned char* pb = smem + p_base_gen + (i % C::P_BUFS) * C::P_BYTES + tid * 16;
 #pragma unroll
       for (int g = 0; g < NP / 8; ++g) {
         uint32_t w[4];
@@ -520,8 +613,6 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     }
 
     // -------------------------------------------------------------- epilogue
-    const int64_t o_split = static_cast<int64_t>(split) * p.n * p.hq * HD;
-    const int64_t l_split = static_cast<int64_t>(split) * p.hq * p.n;
     // row sums over the 128 keys of each tile position
 #pragma unroll
     for (int c = 0; c < NP; ++c) {
@@ -534,10 +625,28 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     const bool landed = ntiles == 0 || mbar_wait(o_final, 0);
     const bool fin = !named_bar_or(!landed || timed_out, 1, NSM);  // uniform: TMEM reads are collective
     if (!landed && tid == 0) set_error(p.err, FOLD_DEVERR_TIMEOUT);
+    // thread c turns row c into its reciprocal sum and output offset (lims/rowf are free now)
+    int* row_off = lims;
+    float* row_inv = rowf;
+    if (tid < NP) {
+      const float L = red[tid] + red[NP + tid] + red[2 * NP + tid] + red[3 * NP + tid];
+      const bool live = fin && L > 0.f && tid < nrows;
+      row_inv[tid] = live ? 1.f / L : 0.f;
+      const int r = tid / G, hq = h * G + (tid - r * G);
+      row_off[tid] = tid < nrows ? (r * p.hq + hq) * HD : -1;
+      if (tid < nrows)
+        p.lse_part[static_cast<int64_t>(split) * p.hq * p.n + static_cast<int64_t>(hq) * p.n + r] =
+            live ? (rowm[tid] + __log2f(L)) * kLn2 : -INFINITY;
+    }
+    named_bar_sync(2, NSM);
+    float inv[NP];
+    int off[NP];
+#pragma unroll
+    for (int c = 0; c < NP; ++c) inv[c] = row_inv[c], off[c] = row_off[c];
     tc_fence_after();
+    float* __restrict__ out = p.o_part + static_cast<int64_t>(split) * p.n * p.hq * HD + tid;
 #pragma unroll
     for (int hh = 0; hh < KU; ++hh) {
-      const int hd = hh * 128 + tid;
 #pragma unroll
       for (int c0 = 0; c0 < NP; c0 += 16) {
         float v[16];
@@ -548,21 +657,9 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int c = c0 + j;
-          if (c < nrows) {
-            const float L = red[c] + red[NP + c] + red[2 * NP + c] + red[3 * NP + c];
-            const int r = c / G, hq = h * G + (c - r * G);
-            p.o_part[o_split + (static_cast<int64_t>(r) * p.hq + hq) * HD + hd] = (fin && L > 0.f) ? v[j] / L : 0.f;
-          }
-        }
+        for (int j = 0; j < 16; ++j)
+          if (off[c0 + j] >= 0) out[off[c0 + j] + hh * 128] = v[j] * inv[c0 + j];
       }
-    }
-    if (tid < nrows) {
-      const float L = red[tid] + red[NP + tid] + red[2 * NP + tid] + red[3 * NP + tid];
-      const int r = tid / G, hq = h * G + (tid - r * G);
-      p.lse_part[l_split + static_cast<int64_t>(hq) * p.n + r] =
-          (fin && L > 0.f) ? (rowm[tid] + __log2f(L)) * kLn2 : -INFINITY;
     }
   }
 
