@@ -50,7 +50,7 @@ METRIC = "us/draft-step (FOLD far-read + merge)"
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="fold", choices=["fold", "reference"])
@@ -65,6 +65,7 @@ def parse():
 # ------------------------------------------------------------------------------ clocks sampler
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    # started 0.3 s before the work so that the first samples already see the load
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -314,9 +315,10 @@ def run_gpu(args):
 
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        # clocks are sampled over a short untimed soak of the same steps and the timed region
+        # clocks are sampled over the timed region and a short untimed run of the same steps before
+        # it (nvidia-smi samples every 100 ms)
         t_soak = time.perf_counter()
-        while graph is not None and time.perf_counter() - t_soak < 0.6:
+        while graph is not None and time.perf_counter() - t_soak < 0.2:
             graph.replay()
             torch.cuda.synchronize()
         barrier()

@@ -61,121 +61,125 @@ __device__ __forceinline__ void load_row(const void* base, int bf16, int64_t off
   }
 }
 
-// Combines the far partials of (t, h) into acc (normalised) and returns their LSE (-inf if none).
-// Lane s holds split s's weight; the partial rows are loaded in batches of independent loads (the
-// partials sit in L2 right after the far read, so latency, not bandwidth, bounds this).
-template <int EPL>
-__device__ __forceinline__ float combine_far(const MergeParams& p, int t, int h, int lane, float (&acc)[EPL]) {
-  constexpr int BATCH = EPL <= 4 ? 16 : 8;
+constexpr int kMergeWarps = 4;  // warps of one block; they split the far partials between them
+constexpr int kSlice = 128;     // head dims per block: 32 lanes x 4 consecutive values
+
+// One block per (row t, query head h, 128-wide slice of the head dims). Lane l holds columns
+// [4l, 4l+4) of the slice. The far partials are log-sum-exp combined: every warp takes a quarter
+// of the splits, loads its partial rows in batches of independent loads (they sit in L2 after
+// the far read) and the four weighted sums meet in shared memory. FINAL merges the result with
+// the window read (fold/kernels.py:94-107) into the bf16 output; otherwise the combined partial
+// itself is written (float32 o and lse).
+template <bool FINAL>
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeParams p, int slices, int hd) {
+  __shared__ float s_acc[kMergeWarps][kSlice];
+  __shared__ float s_w[kMergeWarps];
+  constexpr int BATCH = 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = blockIdx.x % slices, th = blockIdx.x / slices;
+  const int t = th / p.hq, h = th - (th / p.hq) * p.hq;
+  const int width = min(hd, kSlice);
+  const bool active = lane * 4 < width;
+  const int col = slice * kSlice + lane * 4;
+
+  bool has_far = true;
+  if constexpr (FINAL) {
+    const int qlen = p.qsl[1] - p.qsl[0];
+    const int hist = max(p.seq[0] - qlen, 0);
+    has_far = hist - p.window - p.block + 1 + t > 0;  // fold/kernels.py:94-95
+  }
   const float* lf = p.lse_f + static_cast<int64_t>(h) * p.lf_sh + static_cast<int64_t>(t) * p.lf_st;
   float mx = -INFINITY;
-  for (int s = lane; s < p.splits; s += 32) mx = fmaxf(mx, lf[s * p.lf_ss]);
-  mx = warp_max(mx);
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) acc[i] = 0.f;
-  if (mx == -INFINITY) return -INFINITY;
-  float wsum = 0.f;
-  const int64_t base = static_cast<int64_t>(t) * p.of_st + static_cast<int64_t>(h) * p.of_sh + lane * EPL;
-  for (int s0 = 0; s0 < p.splits; s0 += 32) {
-    const int cnt = min(32, p.splits - s0);
-    const float l = lane < cnt ? lf[(s0 + lane) * p.lf_ss] : -INFINITY;
-    const float w = l == -INFINITY ? 0.f : expf(l - mx);  // an empty split carries no mass
-    wsum += w;
-    for (int j = 0; j < cnt; j += BATCH) {
-      float v[BATCH][EPL];
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u) {
-        if (j + u < cnt) {
-          load_row<EPL>(p.o_f, p.of_bf16, base + (s0 + j + u) * p.of_ss, v[u]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < EPL; ++i) v[u][i] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u) {
-        const float wu = __shfl_sync(0xffffffffu, w, (j + u) & 31);
-        if (j + u < cnt) {
-#pragma unroll
-          for (int i = 0; i < EPL; ++i) acc[i] = fmaf(wu, v[u][i], acc[i]);
-        }
-      }
-    }
-  }
-  wsum = warp_sum(wsum);
-  const float inv = 1.f / wsum;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) acc[i] *= inv;
-  return mx + logf(wsum);
-}
-
-template <int EPL>
-__global__ void merge_kernel(const MergeParams p) {
-  const int lane = threadIdx.x & 31;
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (w >= p.n * p.hq) return;
-  const int t = w / p.hq, h = w - (w / p.hq) * p.hq;
-  const int qlen = p.qsl[1] - p.qsl[0];
-  const int hist = max(p.seq[0] - qlen, 0);
-  const bool has_far = hist - p.window - p.block + 1 + t > 0;  // fold/kernels.py:94-95
-  float ol[EPL];
-  load_row<EPL>(p.o_l, 1, static_cast<int64_t>(t) * p.ol_st + static_cast<int64_t>(h) * p.ol_sh + lane * EPL, ol);
-  float y[EPL];
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) y[i] = ol[i];
   if (has_far) {
-    float of[EPL];
-    const float lse_far = combine_far<EPL>(p, t, h, lane, of);
-    if (lse_far != -INFINITY) {
-      const float ll = p.lse_l[static_cast<int64_t>(h) * p.ll_sh + static_cast<int64_t>(t) * p.ll_st];
-      const float lf = lse_far * p.inv_alpha;  // memory log-mass (Eq. 3)
-      const float m = fmaxf(ll, lf);
-      const float wl = expf(ll - m), wf = expf(lf - m);
-      const float inv = 1.f / (wl + wf);
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) y[i] = (wl * ol[i] + wf * of[i]) * inv;
-    }
+    for (int s = lane; s < p.splits; s += 32) mx = fmaxf(mx, lf[s * p.lf_ss]);
+    mx = warp_max(mx);
   }
-  __nv_bfloat16* o = p.out + static_cast<int64_t>(t) * p.out_st + static_cast<int64_t>(h) * p.out_sh + lane * EPL;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float wsum = 0.f;
+  if (mx != -INFINITY) {
+    const int per = (p.splits + kMergeWarps - 1) / kMergeWarps;
+    const int s0 = warp * per, s1 = min(p.splits, s0 + per);
+    const int64_t base = static_cast<int64_t>(t) * p.of_st + static_cast<int64_t>(h) * p.of_sh + col;
+    for (int sb = s0; sb < s1; sb += 32) {
+      const int cnt = min(32, s1 - sb);
+      const float l = lane < cnt ? lf[(sb + lane) * p.lf_ss] : -INFINITY;
+      const float w = l == -INFINITY ? 0.f : expf(l - mx);  // an empty split carries no mass
+      wsum += w;
+      for (int j = 0; j < cnt; j += BATCH) {
+        float v[BATCH][4];
 #pragma unroll
-  for (int i = 0; i < EPL; i += 2) *reinterpret_cast<__nv_bfloat162*>(o + i) = __floats2bfloat162_rn(y[i], y[i + 1]);
-}
-
-template <int EPL>
-__global__ void combine_kernel(const MergeParams p) {
-  const int lane = threadIdx.x & 31;
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (w >= p.n * p.hq) return;
-  const int t = w / p.hq, h = w - (w / p.hq) * p.hq;
-  float acc[EPL];
-  const float lse = combine_far<EPL>(p, t, h, lane, acc);
-  float* o = p.o_out + (static_cast<int64_t>(t) * p.hq + h) * (EPL * 32) + lane * EPL;
+        for (int u = 0; u < BATCH; ++u) {
+          if (active && j + u < cnt) {
+            load_row<4>(p.o_f, p.of_bf16, base + (sb + j + u) * p.of_ss, v[u]);
+          } else {
+            v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+          }
+        }
 #pragma unroll
-  for (int i = 0; i < EPL; i += 2) *reinterpret_cast<float2*>(o + i) = make_float2(acc[i], acc[i + 1]);
-  if (lane == 0) p.lse_out[static_cast<int64_t>(h) * p.n + t] = lse;
+        for (int u = 0; u < BATCH; ++u) {
+          const float wu = __shfl_sync(0xffffffffu, w, (j + u) & 31);
+          if (j + u < cnt) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = fmaf(wu, v[u][i], acc[i]);
+          }
+        }
+      }
+    }
+    wsum = warp_sum(wsum);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s_acc[warp][lane * 4 + i] = acc[i];
+  if (lane == 0) s_w[warp] = wsum;
+  __syncthreads();
+  if (warp != 0) return;
+  float W = 0.f, of[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) {
+    W += s_w[w];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) of[i] += s_acc[w][lane * 4 + i];
+  }
+  const bool any = mx != -INFINITY && W > 0.f;
+  const float inv = any ? 1.f / W : 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) of[i] *= inv;
+  const float lse_far = any ? mx + logf(W) : -INFINITY;
+  if constexpr (FINAL) {
+    if (!active) return;
+    float ol[4];
+    load_row<4>(p.o_l, 1, static_cast<int64_t>(t) * p.ol_st + static_cast<int64_t>(h) * p.ol_sh + col, ol);
+    float y[4] = {ol[0], ol[1], ol[2], ol[3]};
+    if (any) {
+      const float ll = p.lse_l[static_cast<int64_t>(h) * p.ll_sh + static_cast<int64_t>(t) * p.ll_st];
+      const float lfa = lse_far * p.inv_alpha;  // memory log-mass (Eq. 3)
+      const float m = fmaxf(ll, lfa);
+      const float wl = expf(ll - m), wf = expf(lfa - m);
+      const float r = 1.f / (wl + wf);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = (wl * ol[i] + wf * of[i]) * r;
+    }
+    __nv_bfloat16* o = p.out + static_cast<int64_t>(t) * p.out_st + static_cast<int64_t>(h) * p.out_sh + col;
+    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(y[0], y[1]);
+    *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(y[2], y[3]);
+  } else {
+    if (active) {
+      float* o = p.o_out + (static_cast<int64_t>(t) * p.hq + h) * hd + col;
+      *reinterpret_cast<float4*>(o) = make_float4(of[0], of[1], of[2], of[3]);
+    }
+    if (lane == 0 && slice == 0) p.lse_out[static_cast<int64_t>(h) * p.n + t] = lse_far;
+  }
 }
 
 static int merge_launch(const MergeParams& p, int hd, bool combine, cudaStream_t stream) {
-  const int warps = p.n * p.hq;
-  const int threads = 128;
-  const int blocks = (warps + 3) / 4;
-  switch (hd) {
-    case 64:
-      combine ? combine_kernel<2><<<blocks, threads, 0, stream>>>(p) : merge_kernel<2><<<blocks, threads, 0, stream>>>(p);
-      break;
-    case 128:
-      combine ? combine_kernel<4><<<blocks, threads, 0, stream>>>(p) : merge_kernel<4><<<blocks, threads, 0, stream>>>(p);
-      break;
-    case 256:
-      combine ? combine_kernel<8><<<blocks, threads, 0, stream>>>(p) : merge_kernel<8><<<blocks, threads, 0, stream>>>(p);
-      break;
-    case 512:
-      combine ? combine_kernel<16><<<blocks, threads, 0, stream>>>(p)
-              : merge_kernel<16><<<blocks, threads, 0, stream>>>(p);
-      break;
-    default:
-      return fail(FOLD_ERR_UNSUPPORTED, "merge: head size must be 64, 128, 256 or 512");
-  }
+  if (hd < 8 || (hd > kSlice && hd % kSlice) || (hd <= kSlice && hd % 4))
+    return fail(FOLD_ERR_UNSUPPORTED, "merge: head size must be a multiple of 128, or of 4 up to 128");
+  const int slices = hd > kSlice ? hd / kSlice : 1;
+  const int64_t blocks = static_cast<int64_t>(p.n) * p.hq * slices;
+  if (blocks > 2147483647) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge: too many rows");
+  if (combine)
+    merge_kernel<false><<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, stream>>>(p, slices, hd);
+  else
+    merge_kernel<true><<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, stream>>>(p, slices, hd);
   return check_launch(combine ? "combine_kernel" : "merge_kernel");
 }
 
@@ -239,8 +243,8 @@ int fold_combine(const float* o_part, const float* lse_part, int splits, float* 
   using namespace fold;
   if (!o_part || !lse_part || !o_out || !lse_out) return fail(FOLD_ERR_INVALID_ARGUMENT, "combine: null pointer");
   if (n < 1 || hq < 1 || splits < 1) return fail(FOLD_ERR_INVALID_ARGUMENT, "combine: bad sizes");
-  if ((reinterpret_cast<uintptr_t>(o_part) & 7) || (reinterpret_cast<uintptr_t>(o_out) & 7))
-    return fail(FOLD_ERR_ALIGNMENT, "combine: buffers must be 8-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(o_part) & 7) || (reinterpret_cast<uintptr_t>(o_out) & 15) || hd % 4)
+    return fail(FOLD_ERR_ALIGNMENT, "combine: o_part 8-byte and o_out 16-byte aligned, head size a multiple of 4");
   MergeParams p{};
   p.o_f = o_part, p.of_bf16 = 0;
   p.of_ss = static_cast<int64_t>(n) * hq * hd, p.of_st = static_cast<int64_t>(hq) * hd, p.of_sh = hd;
