@@ -50,7 +50,7 @@ METRIC = "us/draft-step (FOLD far-read + merge)"
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="fold", choices=["fold", "reference"])
@@ -225,7 +225,7 @@ def run_gpu(args):
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=30), device_id=dev)
     cfg = CONFIGS[args.config]
     hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
     total = args.warmup + args.steps
@@ -313,14 +313,24 @@ def run_gpu(args):
             for j in range(args.steps):
                 step(args.warmup + j)
 
+    # A short untimed run of the same steps precedes the timed region so that nvidia-smi (100 ms
+    # samples) sees the load. Its length is decided on rank 0 and shared, so that every rank issues
+    # the same collectives.
+    pre = 0
+    if graph is not None:
+        t0 = time.perf_counter()
+        graph.replay()
+        torch.cuda.synchronize()
+        pre = max(1, min(50, int(0.2 / max(time.perf_counter() - t0, 1e-4))))
+    if world > 1:
+        n_pre = torch.tensor([pre], device=dev, dtype=torch.int64)
+        dist.broadcast(n_pre, src=0)
+        pre = int(n_pre.item())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        # clocks are sampled over the timed region and a short untimed run of the same steps before
-        # it (nvidia-smi samples every 100 ms)
-        t_soak = time.perf_counter()
-        while graph is not None and time.perf_counter() - t_soak < 0.2:
+        for _ in range(pre):
             graph.replay()
-            torch.cuda.synchronize()
+        torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0.record(stream)
@@ -345,12 +355,13 @@ def run_gpu(args):
     torch.cuda.synchronize()
     far_ms = f0.elapsed_time(f1) / args.steps
     del far_graph
-    if int(err.item()):
-        raise RuntimeError(f"device error word {int(err.item())}")
-    t = torch.tensor([ms, far_ms], device=dev, dtype=torch.float64)
+    # every rank takes part in the reduction before any rank may raise (same collectives everywhere)
+    t = torch.tensor([ms, far_ms, float(err.item())], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, far_ms = float(t[0]), float(t[1])
+    if int(t[2]):
+        raise RuntimeError(f"device error word {int(t[2])} on some rank")
     us_step = 1000.0 * ms / args.steps
 
     # algorithmic bytes of one far-read launch on this rank: its K/V rows + q + partials
