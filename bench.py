@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch the timed steps from Python, not as a CUDA graph")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: how the per-rank partials meet (peer-to-peer kernel, or NCCL all-gather + merge)")
     return ap.parse_args()
 
 
@@ -215,7 +217,7 @@ def run_gpu(args):
 
     from fold_b200 import kernels
     from fold_b200.rope import default_inv_freq, rope_table
-    from fold_b200.shard import ShardPlan, unpack_partials
+    from fold_b200.shard import PeerExchange, ShardPlan, unpack_partials
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -269,6 +271,7 @@ def run_gpu(args):
     o_mine, lse_mine = send[: B * hq * hd].view(B, hq, hd), send[B * hq * hd:].view(hq, B)
     scale = hd ** -0.5 * ALPHA
     stream = torch.cuda.current_stream(dev)
+    peer = PeerExchange(n=B, hq=hq, hd=hd, device=dev) if world > 1 and args.exchange == "p2p" else None
 
     def far(i):
         kernels.far_read(q_all[i], qsl, seq_all[i: i + 1], side, o_part, lse_part, window=W, block=B,
@@ -281,7 +284,9 @@ def run_gpu(args):
                            pos_lo=pos_lo, skip_foreign=world > 1, err=err)
         seq = seq_all[i: i + 1]
         far(i)
-        if world > 1:
+        if peer is not None:
+            peer.merge(o_part, lse_part, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=ALPHA, err=err)
+        elif world > 1:
             kernels.combine(o_part, lse_part, o_mine, lse_mine)
             dist.all_gather_into_tensor(recv, send)
             o_all, lse_all = unpack_partials(recv, world, B, hq, hd)
@@ -405,6 +410,9 @@ def run_gpu(args):
             "config": {"workload": cfg["name"], "context": cfg["ctx"], "window": W, "block": B, "heads_q": hq,
                        "heads_kv": hkv, "head_dim": hd, "alpha": ALPHA, "splits": splits,
                        "parallelism": f"seq-shard{world}" if world > 1 else "single",
+                       "exchange": None if world == 1 else (
+                           "peer-to-peer kernel (NVLink stores + flags, combine and merge fused)" if peer is not None
+                           else "combine + NCCL all-gather + merge"),
                        "timing": "eager launches" if args.eager else "CUDA graph of the K timed steps",
                        "l2": "inputs larger than L2 (side cache %.0f MB per GPU)" % (side.numel() * 2 / 1e6)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -413,7 +421,7 @@ def run_gpu(args):
                          "kernel_timing": "burst: the far read alone, one graph of K launches after idle",
                          "kernel_us_sustained": round(far_sustained_ms * 1000, 3),
                          "algorithmic_bytes": int(alg), "traffic": traffic},
-            "gpu_launches": args.steps * (3 if world == 1 else 4),
+            "gpu_launches": args.steps * (3 if world == 1 or peer is not None else 4),
             "clocks": clocks.summary(),
             "e2e": e2e,
         }
@@ -421,6 +429,8 @@ def run_gpu(args):
             line["cpu_baseline"] = cpu_baseline(cfg, args.seed)
         print(json.dumps(line), flush=True)
     del graph
+    if peer is not None:
+        peer.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -444,7 +454,7 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
                        shard_len=plan.held if world > 1 else None)
     ws.side = side  # the same resident side cache as the kernel leg
     ws._table = table
-    sharded = ShardedFarMemory(plan, ws) if world > 1 else None
+    sharded = ShardedFarMemory(plan, ws, exchange=args.exchange) if world > 1 else None
     gen = torch.Generator().manual_seed(args.seed + 99)
     max_acc = int(acc.max())
     h_q = torch.randn((total, B, hq, hd), generator=gen).to(torch.bfloat16).pin_memory()
@@ -506,6 +516,8 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    if sharded is not None and sharded.peer is not None:
+        sharded.peer.close()
     return {"value": round(1000.0 * float(ms) / args.steps, 3), "unit": "us/draft-step",
             "h2d_bytes_per_step": int(h2d / args.steps), "d2h_bytes_per_step": int(d2h / args.steps),
             "api": "FoldWorkspace.append/read_far + kernels.merge (fold_b200 C-ABI), pinned host buffers"}

@@ -1,10 +1,11 @@
 /* C-ABI of the FOLD drafter-attention hot path on B200 (sm_100a).
  *
  * Every entry point takes plain device pointers (owned by the caller), sizes and strides in
- * elements, and a CUDA stream (`stream`, a cudaStream_t passed as void*). None of them allocates
- * device memory, synchronises the host or reads a device value on the host: the lengths of a
- * draft step (query_start_loc, seq_lens) are read on the device, so every call can be captured
- * in a CUDA graph. Each returns FOLD_OK (0) or a fold_status; fold_last_error() gives the detail
+ * elements, and a CUDA stream (`stream`, a cudaStream_t passed as void*). None of the step entry
+ * points allocates device memory, synchronises the host or reads a device value on the host: the
+ * lengths of a draft step (query_start_loc, seq_lens) are read on the device, so every call can be
+ * captured in a CUDA graph (the setup calls fold_exchange_create/open/destroy do allocate and
+ * synchronise). Each returns FOLD_OK (0) or a fold_status; fold_last_error() gives the detail
  * of the last failure on the calling thread.
  *
  * Conventions (fold/kernels.py:1-13 of the reference): batch 1; qlen = qsl[1] - qsl[0];
@@ -40,7 +41,7 @@ enum fold_status {
 
 #define FOLD_DEVERR_APPEND_RANGE 1 /* an append/gather position lies outside the cache */
 #define FOLD_DEVERR_ROPE_RANGE 2   /* |rotation offset| beyond the rope table (offset clamped) */
-#define FOLD_DEVERR_TIMEOUT 4      /* a pipeline wait of the far read gave up */
+#define FOLD_DEVERR_TIMEOUT 4      /* a pipeline wait of the far read, or a wait for a peer, gave up */
 #define FOLD_DEVERR_CAPACITY 8     /* far_len exceeds the side cache's capacity */
 
 const char* fold_status_string(int status);
@@ -153,6 +154,46 @@ int fold_far_read_merge_static(const void* q, int64_t q_stride_tok, int64_t q_st
                                int64_t out_stride_head, int splits, int n, int hq, int hkv, int hd, int window,
                                int block, int far_distance, float softmax_scale, float inv_alpha, int* err,
                                void* stream);
+
+/* ---- Sequence-sharded far memory: peer-to-peer exchange of the per-rank partials ----
+ *
+ * With the side cache partitioned by position across the GPUs of one node (one process per GPU),
+ * every rank reads its chunk with fold_far_read and the ranks' partials must be combined. The
+ * reference runs on one GPU and has no counterpart; these entry points replace an all-gather of
+ * the partials (ncclAllGather) followed by fold_merge with one kernel that combines this rank's
+ * splits, stores the result into every rank's receive buffer over NVLink, raises a flag per item,
+ * waits for the peers' flags (at most 2 s; then FOLD_DEVERR_TIMEOUT, and later calls on this
+ * exchange stop waiting) and merges. Setup is collective: every rank calls fold_exchange_create,
+ * the ranks share their handles (any host transport, e.g. an all-gather of the 64-byte handles),
+ * and every rank calls fold_exchange_open with all handles in rank order. The exchange allocates
+ * its device region at creation; the step itself allocates nothing and is graph-capturable.
+ * Every rank must make the same sequence of fold_exchange_merge calls with the same n, hq and hd
+ * (one call per layer per draft step); calls on one exchange must be issued in one stream order. */
+#define FOLD_EXCHANGE_HANDLE_BYTES 64
+
+/* Creates this rank's exchange on the current device for partials of up to part_floats floats
+ * (n*hq*hd + hq*n at the largest step; a multiple of 4) and max_items items (n*hq*ceil(hd/128)).
+ * Writes the opaque exchange to *exchange and this rank's FOLD_EXCHANGE_HANDLE_BYTES-byte IPC
+ * handle to `handle`. world <= 8. */
+int fold_exchange_create(int world, int rank, int64_t part_floats, int max_items, void** exchange, void* handle);
+
+/* Maps the other ranks' regions: `handles` holds world handles of FOLD_EXCHANGE_HANDLE_BYTES
+ * bytes, in rank order (this rank's own entry is ignored). */
+int fold_exchange_open(void* exchange, const void* handles);
+
+/* Unmaps the peers and frees this rank's region. Call after the last merge has completed on every
+ * rank (e.g. after a device synchronisation and a host barrier). */
+int fold_exchange_destroy(void* exchange);
+
+/* The step: o_part [splits, n, hq, hd] / lse_part [splits, hq, n] are this rank's far-read
+ * partials (float32, contiguous, as written by fold_far_read over this rank's chunk); the window
+ * read o_l, lse_l and the output `out` are as in fold_merge. Every rank writes the same merged
+ * output. Replaces, on each rank, fold_combine + the all-gather + fold_merge of the partials. */
+int fold_exchange_merge(void* exchange, const float* o_part, const float* lse_part, int splits, const void* o_l,
+                        int64_t ol_stride_tok, int64_t ol_stride_head, const float* lse_l, int64_t ll_stride_head,
+                        int64_t ll_stride_tok, void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        const int* qsl, const int* seq_lens, int n, int hq, int hd, int window, int block,
+                        float inv_alpha, int* err, void* stream);
 
 #ifdef __cplusplus
 }

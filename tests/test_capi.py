@@ -62,3 +62,19 @@ def test_kernel_selection_validates():
         _lib.call("fold_far_read_select_kernel", 7)
     kernels.select_far_read_kernel("tc")
     kernels.select_far_read_kernel("auto")
+
+
+def test_exchange_rejects_bad_arguments_without_a_gpu():
+    import ctypes
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(64)
+    with pytest.raises(FoldError, match="world"):
+        _lib.call("fold_exchange_create", 9, 0, 64, 1, ctypes.byref(ptr), ctypes.cast(buf, ctypes.c_void_p))
+    with pytest.raises(FoldError, match="world"):
+        _lib.call("fold_exchange_create", 2, 2, 64, 1, ctypes.byref(ptr), ctypes.cast(buf, ctypes.c_void_p))
+    with pytest.raises(FoldError, match="multiple of 4"):
+        _lib.call("fold_exchange_create", 2, 0, 62, 1, ctypes.byref(ptr), ctypes.cast(buf, ctypes.c_void_p))
+    with pytest.raises(FoldError, match="null pointer"):
+        _lib.call("fold_exchange_merge", None, None, None, 1, None, 0, 0, None, 0, 0, None, 0, 0, None, None, 1, 1,
+                  128, 1, 1, 0.5, None, None)
+    _lib.call("fold_exchange_destroy", None)  # destroying nothing is a no-op

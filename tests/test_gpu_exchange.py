@@ -1,0 +1,101 @@
+"""The peer exchange kernel (fold_exchange_merge) on one GPU, as a group of one rank: its combine
+of the split partials, its push/flag/wait protocol (local here) and its merge must give exactly
+the merge kernel's output, and match the oracle's combine + merge; repeated launches and graph
+replays advance the device epoch without a host input. The multi-rank protocol runs in
+test_gpu_shard.py when 2 GPUs are present."""
+import numpy as np
+import pytest
+import torch
+
+from fold_b200 import kernels
+from fold_b200.errors import FoldError
+from fold_b200.shard import PeerExchange
+from oracle import fold_oracle as fo
+from tests.helpers import OUT_ATOL, to64
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+
+def partials(seed, S, n, hq, hd, empty_every=5):
+    g = torch.Generator().manual_seed(seed)
+    o = torch.randn((S, n, hq, hd), generator=g)
+    lse = torch.randn((S, hq, n), generator=g) * 3 + 8
+    lse.view(-1)[::empty_every] = -float("inf")  # empty splits carry no mass
+    o_l = torch.randn((n, hq, hd), generator=g).to(torch.bfloat16)
+    lse_l = torch.randn((hq, n), generator=g) + 6
+    return [t.cuda() for t in (o, lse, o_l, lse_l)]
+
+
+@pytest.mark.parametrize("S,n,hq,hd,hist", [(18, 10, 32, 128, 131062), (37, 16, 16, 256, 262128), (5, 3, 4, 64, 2100),
+                                            (7, 10, 8, 128, 2050)])
+def test_single_rank_exchange_equals_merge_kernel(S, n, hq, hd, hist):
+    W, B, alpha = 2048, n, 2.0
+    o, lse, o_l, lse_l = partials(S + n, S, n, hq, hd)
+    qsl = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+    seq = torch.tensor([hist + n], dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want = torch.empty((n, hq, hd), dtype=torch.bfloat16, device="cuda")
+    kernels.merge(o_l, lse_l, o, lse, want, qsl, seq, window=W, block=B, alpha=alpha)
+    ex = PeerExchange(n=n, hq=hq, hd=hd)
+    try:
+        got = torch.empty_like(want)
+        ex.merge(o, lse, o_l, lse_l, got, qsl, seq, window=W, block=B, alpha=alpha, err=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert torch.equal(got, want)
+        o_f, lse_f = fo.combine(to64(o), to64(lse))
+        ref = fo.merge(to64(o_l), to64(lse_l), o_f, lse_f, hist, W, B, alpha)
+        assert np.abs(to64(got) - ref).max() <= OUT_ATOL
+    finally:
+        ex.close()
+
+
+def test_exchange_epochs_advance_across_calls_and_graph_replays():
+    S, n, hq, hd, W, B, hist = 18, 10, 32, 128, 2048, 10, 50000
+    qsl = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+    seq = torch.tensor([hist + n], dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    steps = [partials(100 + i, S, n, hq, hd) for i in range(3)]
+    want = []
+    for o, lse, o_l, lse_l in steps:
+        w = torch.empty((n, hq, hd), dtype=torch.bfloat16, device="cuda")
+        kernels.merge(o_l, lse_l, o, lse, w, qsl, seq, window=W, block=B, alpha=2.0)
+        want.append(w)
+    ex = PeerExchange(n=n, hq=hq, hd=hd)
+    outs = [torch.empty((n, hq, hd), dtype=torch.bfloat16, device="cuda") for _ in steps]
+    try:
+        for _ in range(3):  # eager calls: epochs 1..9
+            for (o, lse, o_l, lse_l), out in zip(steps, outs):
+                ex.merge(o, lse, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=2.0, err=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert all(torch.equal(a, b) for a, b in zip(outs, want))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for (o, lse, o_l, lse_l), out in zip(steps, outs):
+                ex.merge(o, lse, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=2.0, err=err)
+        for out in outs:
+            out.zero_()
+        for _ in range(5):  # 15 more epochs, both parities, no host input
+            graph.replay()
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert all(torch.equal(a, b) for a, b in zip(outs, want))
+        del graph
+    finally:
+        ex.close()
+
+
+def test_exchange_rejects_a_larger_step_than_created_for():
+    ex = PeerExchange(n=4, hq=8, hd=128)
+    try:
+        o, lse, o_l, lse_l = partials(1, 3, 6, 8, 128)
+        qsl = torch.tensor([0, 6], dtype=torch.int32, device="cuda")
+        seq = torch.tensor([9000], dtype=torch.int32, device="cuda")
+        with pytest.raises(FoldError, match="larger"):
+            ex.merge(o, lse, o_l, lse_l, torch.empty_like(o_l), qsl, seq, window=2048, block=6, alpha=2.0)
+    finally:
+        ex.close()

@@ -66,36 +66,76 @@ def workspace(p, device, plan=None):
     return plan.workspace(dummy, p["W"], p["n"], inv_freq=inv, far_distance=p["W"] + p["n"], num_heads=p["hq"])
 
 
-def worker(rank, world, port, q):
+def worker(rank, world, port, q, exchange):
     import torch.distributed as dist
 
     from fold_b200.shard import ShardedFarMemory, ShardPlan
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
+    sharded = None
     try:
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=device)
         p = inputs(device)
         plan = ShardPlan.even(p["length"], world, rank)
         ws = workspace(p, device, plan)
-        out = step(p, ws, device, ShardedFarMemory(plan, ws))
-        q.put((rank, "ok", out.numpy()))
+        sharded = ShardedFarMemory(plan, ws, exchange=exchange)
+        out = step(p, ws, device, sharded)
+        replayed = None
+        if exchange == "p2p":
+            replayed = replay(p, ws, device, sharded)
+        q.put((rank, "ok", (out.numpy(), replayed)))
     except Exception as e:
         q.put((rank, "error", repr(e)))
     finally:
+        if sharded is not None and sharded.peer is not None:
+            sharded.peer.close()
         if dist.is_initialized():
             dist.destroy_process_group()
 
 
-def test_two_gpu_sharded_read_matches_single_gpu():
+def replay(p, ws, device, sharded, steps=4, replays=6):
+    """The far read + exchange of `steps` draft steps captured in one CUDA graph and replayed: the
+    device epochs and buffer parities advance with no host input; every replay must give the eager
+    result again."""
+    qsl = torch.tensor([0, p["n"]], dtype=torch.int32, device=device)
+    seq = torch.tensor([p["length"]], dtype=torch.int32, device=device)
+    outs = [torch.empty((p["n"], p["hq"], p["hd"]), device=device, dtype=torch.bfloat16) for _ in range(steps)]
+    scale = p["hd"] ** -0.5
+
+    def body():
+        for out in outs:
+            o_part, lse_part = sharded.step(p["q"], qsl, seq, scale)
+            sharded.merge(p["o_l"], p["lse_l"], o_part, lse_part, out, qsl, seq)
+
+    body()
+    torch.cuda.synchronize(device)
+    first = [o.clone() for o in outs]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    same = True
+    for _ in range(replays):
+        for o in outs:
+            o.zero_()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        same = same and all(torch.equal(a, b) for a, b in zip(outs, first))
+    del graph
+    ws.check()
+    return same
+
+
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_two_gpu_sharded_read_matches_single_gpu(exchange):
     device = torch.device("cuda", 0)
     p = inputs(device)
     want = step(p, workspace(p, device), device).numpy()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for pr in procs:
         pr.start()
     res = dict((r, (s, x)) for r, s, x in (q.get(timeout=300) for _ in range(2)))
@@ -103,4 +143,9 @@ def test_two_gpu_sharded_read_matches_single_gpu():
         pr.join(timeout=60)
     for r in (0, 1):
         assert res[r][0] == "ok", res[r]
-        assert np.abs(res[r][1] - want).max() <= 2e-2
+        out, replayed = res[r][1]
+        assert np.abs(out - want).max() <= 2e-2
+        if exchange == "p2p":
+            assert replayed, "graph replays of the peer exchange changed the output"
+    # both ranks hold the same merged output
+    assert np.array_equal(res[0][1][0], res[1][1][0])

@@ -17,7 +17,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from fold_b200.shard import ShardPlan, exchange_partials, pack_partial, unpack_partials
+from fold_b200.shard import ShardPlan, exchange_partials, gather_handles, pack_partial, unpack_partials
 from oracle import fold_oracle as fo
 
 
@@ -54,6 +54,10 @@ def worker(rank, world, port, mode, out_q):
         o, lse = rank_partial(p, plan)
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 fails before the exchange")
+        if mode == "handles":
+            mine = bytes((rank * 37 + i) % 256 for i in range(64))
+            out_q.put((rank, "ok", gather_handles(mine)))
+            return
         o_all, lse_all = exchange_partials(torch.from_numpy(o).float(), torch.from_numpy(lse).float())
         out_q.put((rank, "ok", (o_all.numpy().astype(np.float64), lse_all.numpy().astype(np.float64))))
     except Exception as e:  # reported to the parent, which decides what was expected
@@ -125,3 +129,13 @@ def test_failed_rank_makes_the_exchange_fail_not_hang():
     results = run(2, "fail")
     assert results[1][0] == "error" and "fails before the exchange" in results[1][1]
     assert results[0][0] == "error", results[0]
+
+
+def test_exchange_handles_are_gathered_in_rank_order():
+    """The peer exchange's setup shares every rank's 64-byte IPC handle; every rank must receive all
+    of them, concatenated in rank order."""
+    world = 2
+    results = run(world, "handles")
+    want = b"".join(bytes((r * 37 + i) % 256 for i in range(64)) for r in range(world))
+    for r in range(world):
+        assert results[r] == ("ok", want)
