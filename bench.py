@@ -233,7 +233,7 @@ def run_gpu(args):
     total = args.warmup + args.steps
     acc, H = plan_steps(cfg, total, args.seed)
     length = int(H[-1] + acc[-1]) + B  # every position any step appends or reads
-    plan = ShardPlan.even(length, world, rank)
+    plan = ShardPlan.for_far(length, W, B, world, rank)
     pos_lo, held = plan.pos_lo, plan.held
     pages = -(-max(held, 1) // 256) + 1
 
@@ -448,7 +448,7 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
     total = args.warmup + args.steps
     dummy = torch.zeros((1, hkv, 16, 2 * hd), device=dev, dtype=torch.bfloat16)
-    plan = ShardPlan.even(length, world, rank)
+    plan = ShardPlan.for_far(length, W, B, world, rank)
     ws = FoldWorkspace(dummy, W, B, length, inv_freq=torch.ones(hd // 2, device=dev), far_distance=W + B,
                        alpha=ALPHA, num_heads=hq, splits=splits, pos_lo=plan.pos_lo,
                        shard_len=plan.held if world > 1 else None)

@@ -2,23 +2,31 @@
 // the merge after it, for a side cache sharded by position across the GPUs of one node.
 //
 // Each rank owns one device region, mapped into every other rank's address space with CUDA IPC:
-//   recv  float32 [2 parities][world][part_floats]   partials pushed by every rank
-//   flags uint32  [world][max_items]                  epoch at which rank r pushed item i
-//   ctr   uint32  [4]: last completed epoch, blocks done in this launch, poisoned
-// One launch of exchange_merge_kernel on every rank (all ranks make the same sequence of calls):
-//   1. per item (row t, query head h, 128-column slice): combine this rank's split partials
-//      (log-sum-exp), store the result into the recv slot [parity][rank] of EVERY rank (NVLink
-//      stores into the peers' memory), fence, and raise flag [rank][item] on every rank;
-//   2. per item: wait until every rank's flag for the item reaches this epoch (bounded wait), then
-//      merge the world partials with the window read and write the bf16 output.
+//   recv  [2 parities][world source ranks][max_items] records of kRecordBytes
+//   ctr   uint32 [4]: last completed epoch, blocks done in this launch, poisoned
+// A record holds one item (row t, query head h, 128-column slice) of one rank's combined partial
+// in 16-byte lines {x, epoch, y, epoch}: 64 lines of o (lane l owns lines 2l and 2l+1, i.e.
+// columns 4l..4l+3) and one line with the LSE. Every 8-byte half of a line pairs a value with
+// the epoch that wrote it, and aligned 8-byte stores and loads are single-copy atomic, so a reader
+// that sees the current epoch in both halves of every line it needs has the current data: no
+// fence and no separate flag (the low-latency line format that NCCL's LL protocol also uses).
+//
+// One launch of exchange_merge_kernel on every rank (all ranks make the same sequence of calls);
+// block b handles items b, b + grid, ...; per item:
+//   1. the block combines this rank's split partials (log-sum-exp) into registers of warp 0;
+//   2. warp 0 stores the item's record into slot [parity][this rank] of every other rank (NVLink
+//      stores into the peers' memory);
+//   3. warp 0 polls its own slots [parity][r] for the item until every line carries this epoch
+//      (bounded wait), and merges the world partials (rank order, so that every rank computes the
+//      same output) with the window read.
 // The epoch is a device counter: every launch uses ctr[0] + 1, and its last block to finish
-// stores it, so graph replays need no host input. Data slots alternate between two parities: a
-// rank can be at most one epoch ahead of a peer that is still reading (its own epoch-e+1 wait
-// needs the peer's epoch-e+1 push, which the peer issues only after its epoch-e launch is done).
+// stores it, so graph replays need no host input. Records alternate between two parities: a rank
+// writes epoch e + 2 into a peer's slot only after its epoch-e+1 launch read the peer's epoch-e+1
+// records, which the peer wrote after its epoch-e launch (the last reader of that slot) ended.
 //
 // No counterpart in the reference (one GPU); it replaces an all-gather of the partials (NCCL)
 // followed by the merge kernel. No TMA and no bulk copies are used: plain vector stores to peer
-// memory, release/acquire flags at system scope.
+// memory and volatile polling loads of local memory.
 #include <cuda_bf16.h>
 
 #include <cstring>
@@ -35,11 +43,14 @@ constexpr int kMaxRanks = 8;
 // marks the exchange poisoned (later launches do not wait at all) and merges what it has.
 constexpr uint64_t kPeerWaitTimeoutNs = 2000000000ull;
 
+constexpr int kLinesPerItem = 2 * 32 + 1;  // 64 lines of o + 1 line of LSE
+constexpr int kRecordBytes = kLinesPerItem * 16;
+
 struct Exchange {
   int world = 0, rank = 0, device = -1;
-  int64_t part_floats = 0;  // floats of one rank's partial: n*hq*hd + hq*n at the largest shape
-  int max_items = 0;        // items (row, q head, 128-column slice) at the largest shape
-  size_t bytes = 0, off_flags = 0, off_ctr = 0;
+  int64_t part_floats = 0;  // floats of one rank's partial at the largest step: n*hq*hd + hq*n
+  int max_items = 0;        // items (row, q head, 128-column slice) at the largest step
+  size_t bytes = 0, off_ctr = 0;
   char* base = nullptr;           // this rank's region
   char* peer[kMaxRanks] = {};     // every rank's region in this process's address space
   bool opened[kMaxRanks] = {};    // mapped with cudaIpcOpenMemHandle (to be closed)
@@ -48,39 +59,56 @@ struct Exchange {
 
 struct ExParams {
   MergeParams m;  // split partials (o_f/lse_f, float32 contiguous) and the window read / output
-  float* recv[kMaxRanks];
-  uint32_t* flags[kMaxRanks];
-  const float* my_recv;
-  const uint32_t* my_flags;
+  char* recv[kMaxRanks];  // every rank's record area
+  const char* my_recv;
   uint32_t* ctr;
-  int64_t part_floats;
   int max_items, items, slices, hd;
   int world, rank;
   int* err;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_line(void* p, float x, float y, uint32_t flag) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(x)), "r"(flag),
+               "r"(__float_as_uint(y)), "r"(flag)
+               : "memory");
 }
+__device__ __forceinline__ uint4 ld_line(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ bool line_is(const uint4& v, uint32_t flag) { return v.y == flag && v.w == flag; }
 
-// Waits until *flag has reached `epoch` (wrap-safe). False when the exchange is poisoned or the
-// wait ran out of time (kPeerWaitTimeoutNs on the global timer; independently of the timer, after
-// kPeerWaitMaxPolls polls, which take far longer than that).
+// A wait for a peer's record gives up after kPeerWaitTimeoutNs on the global timer, or
+// independently of the timer after kPeerWaitMaxPolls polls (which take far longer than that).
 constexpr uint32_t kPeerWaitMaxPolls = 1u << 26;
-__device__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, const uint32_t* poisoned) {
+
+// Polls this lane's lines of one record until they carry `epoch`. False when the exchange is
+// poisoned or the wait ran out.
+__device__ __forceinline__ bool read_record(const char* rec, int lane, bool active, uint32_t epoch, const uint32_t* poisoned,
+                            float (&o)[4], float& lse) {
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 0; it < kPeerWaitMaxPolls; ++it) {
-    if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    const uint4 c = ld_line(rec + 64 * 16);
+    uint4 a = c, b = c;
+    if (active) {
+      a = ld_line(rec + (2 * lane) * 16);
+      b = ld_line(rec + (2 * lane + 1) * 16);
+    }
+    if (line_is(a, epoch) && line_is(b, epoch) && line_is(c, epoch)) {
+      o[0] = __uint_as_float(a.x), o[1] = __uint_as_float(a.z);
+      o[2] = __uint_as_float(b.x), o[3] = __uint_as_float(b.z);
+      lse = __uint_as_float(c.x);
+      return true;
+    }
     if ((it & 31u) == 31u) {
       if (ld_relaxed_gpu(poisoned)) return false;
       if (globaltimer() - t0 > kPeerWaitTimeoutNs) return false;
@@ -95,77 +123,83 @@ __global__ void __launch_bounds__(kMergeWarps * 32) exchange_merge_kernel(const 
   __shared__ uint32_t s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const MergeParams& m = p.m;
+  // the epoch load is in flight while the first combine loads the partials; combine_slice's
+  // barrier publishes s_epoch
   if (threadIdx.x == 0) s_epoch = ld_relaxed_gpu(p.ctr) + 1;
-  __syncthreads();
-  const uint32_t epoch = s_epoch;
-  const int64_t slot = (static_cast<int64_t>(epoch & 1u) * p.world + p.rank) * p.part_floats;
   const bool active = lane * 4 < min(p.hd, kSlice);
-  const int64_t lse_base = static_cast<int64_t>(m.n) * m.hq * p.hd;
+  const uint32_t* poisoned = p.ctr + 2;
+  uint32_t epoch = 0;
 
-  // 1. combine this rank's splits of each item and push the result to every rank
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     const int slice = item % p.slices, th = item / p.slices;
     const int t = th / m.hq, h = th - (th / m.hq) * m.hq;
     const int col = slice * kSlice + lane * 4;
     float of[4], lse_far;
     combine_slice(m, t, h, col, active, true, sums, of, lse_far);
+    epoch = s_epoch;
     if (warp == 0) {
-      const int64_t o_off = slot + (static_cast<int64_t>(t) * m.hq + h) * p.hd + col;
-      const int64_t l_off = slot + lse_base + static_cast<int64_t>(h) * m.n + t;
-      // every slice of (t, h) stores the same LSE, so that each item's flag covers what its
-      // reader loads
+      const int par = static_cast<int>(epoch & 1u);
+      // window read first: its loads overlap the pushes and the wait
+      float ol[4] = {0.f, 0.f, 0.f, 0.f};
+      if (active) load_row<4>(m.o_l, 1, static_cast<int64_t>(t) * m.ol_st + static_cast<int64_t>(h) * m.ol_sh + col, ol);
+      const float ll = m.lse_l[static_cast<int64_t>(h) * m.ll_sh + static_cast<int64_t>(t) * m.ll_st];
+      // push this rank's record of the item to every other rank
+      const int64_t mine = ((static_cast<int64_t>(par) * p.world + p.rank) * p.max_items + item) * kRecordBytes;
       for (int r = 0; r < p.world; ++r) {
-        if (active) *reinterpret_cast<float4*>(p.recv[r] + o_off) = make_float4(of[0], of[1], of[2], of[3]);
-        if (lane == 0) p.recv[r][l_off] = lse_far;
+        if (r == p.rank) continue;
+        char* rec = p.recv[r] + mine;
+        if (active) {
+          st_line(rec + (2 * lane) * 16, of[0], of[1], epoch);
+          st_line(rec + (2 * lane + 1) * 16, of[2], of[3], epoch);
+        }
+        if (lane == 0) st_line(rec + 64 * 16, lse_far, lse_far, epoch);
       }
-      __threadfence_system();
-      __syncwarp();
-      if (lane < p.world) st_release_sys(p.flags[lane] + static_cast<int64_t>(p.rank) * p.max_items + item, epoch);
+      // every rank's partial of the item, in rank order
+      float o_r[kMaxRanks][4], lse_r[kMaxRanks];
+      bool ok = true;
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        lse_r[r] = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o_r[r][i] = of[i];
+        if (r < p.world && r != p.rank) {
+          const char* rec = p.my_recv + ((static_cast<int64_t>(par) * p.world + r) * p.max_items + item) * kRecordBytes;
+          if (!read_record(rec, lane, active, epoch, poisoned, o_r[r], lse_r[r])) {
+            ok = false;
+            lse_r[r] = -INFINITY;
+          }
+        } else if (r == p.rank) {
+          lse_r[r] = lse_far;
+        }
+      }
+      if (!__all_sync(0xffffffffu, ok) && lane == 0) {
+        set_error(p.err, FOLD_DEVERR_TIMEOUT);
+        atomicExch(p.ctr + 2, 1u);
+      }
+      // log-sum-exp over the ranks (lse_r is the same in every lane)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) mx = fmaxf(mx, lse_r[r]);  // ranks >= world hold -inf
+      float W = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (mx != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+          const float w = lse_r[r] == -INFINITY ? 0.f : expf(lse_r[r] - mx);
+          W += w;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i] = fmaf(w, o_r[r][i], acc[i]);
+        }
+      }
+      const bool any = mx != -INFINITY && W > 0.f && row_has_far(m, t);
+      const float inv = any ? 1.f / W : 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] *= inv;
+      if (active) merge_store_loaded(m, t, h, col, acc, any ? mx + logf(W) : -INFINITY, ol, ll);
     }
     __syncthreads();  // `sums` is reused by the next item
   }
 
-  // 2. per item (one warp each): wait for every rank's partial, merge with the window read
-  const uint32_t* poisoned = p.ctr + 2;
-  for (int item = blockIdx.x * kMergeWarps + warp; item < p.items; item += gridDim.x * kMergeWarps) {
-    const int slice = item % p.slices, th = item / p.slices;
-    const int t = th / m.hq, h = th - (th / m.hq) * m.hq;
-    const int col = slice * kSlice + lane * 4;
-    bool ok = true;
-    if (lane < p.world) ok = wait_epoch(p.my_flags + static_cast<int64_t>(lane) * p.max_items + item, epoch, poisoned);
-    if (!__all_sync(0xffffffffu, ok)) {
-      if (lane == 0) {
-        set_error(p.err, FOLD_DEVERR_TIMEOUT);
-        atomicExch(p.ctr + 2, 1u);
-      }
-    }
-    __syncwarp();
-    const int64_t base = static_cast<int64_t>(epoch & 1u) * p.world * p.part_floats;
-    const float l = lane < p.world
-                        ? __ldcg(p.my_recv + base + lane * p.part_floats + lse_base + static_cast<int64_t>(h) * m.n + t)
-                        : -INFINITY;
-    const float mx = warp_max(l);
-    const float w = l == -INFINITY ? 0.f : expf(l - mx);
-    const float W = warp_sum(w);
-    float of[4] = {0.f, 0.f, 0.f, 0.f};
-    const int64_t o_off = base + (static_cast<int64_t>(t) * m.hq + h) * p.hd + col;
-    for (int r = 0; r < p.world; ++r) {
-      const float wr = __shfl_sync(0xffffffffu, w, r);
-      if (active && wr > 0.f) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(p.my_recv + o_off + r * p.part_floats));
-        of[0] = fmaf(wr, v.x, of[0]), of[1] = fmaf(wr, v.y, of[1]);
-        of[2] = fmaf(wr, v.z, of[2]), of[3] = fmaf(wr, v.w, of[3]);
-      }
-    }
-    const bool any = mx != -INFINITY && W > 0.f && row_has_far(m, t);
-    const float inv = any ? 1.f / W : 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) of[i] *= inv;
-    if (active) merge_store(m, t, h, col, of, any ? mx + logf(W) : -INFINITY);
-  }
-
   // the last block of the launch publishes the epoch for the next launch
-  __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     if (atomicAdd(p.ctr + 1, 1u) == gridDim.x - 1) {
@@ -196,8 +230,7 @@ int fold_exchange_create(int world, int rank, int64_t part_floats, int max_items
   Exchange* ex = new (std::nothrow) Exchange();
   if (!ex) return fail(FOLD_ERR_INVALID_ARGUMENT, "exchange: out of host memory");
   ex->world = world, ex->rank = rank, ex->part_floats = part_floats, ex->max_items = max_items;
-  ex->off_flags = round_up(sizeof(float) * 2 * static_cast<size_t>(world) * part_floats, 256);
-  ex->off_ctr = ex->off_flags + round_up(sizeof(uint32_t) * static_cast<size_t>(world) * max_items, 256);
+  ex->off_ctr = round_up(static_cast<size_t>(2) * world * max_items * kRecordBytes, 256);
   ex->bytes = ex->off_ctr + 256;
   int st = current_device(&ex->device);
   if (!st) st = check_cuda(cudaMalloc(&ex->base, ex->bytes), "exchange: cudaMalloc");
@@ -295,19 +328,16 @@ int fold_exchange_merge(void* exchange, const float* o_part, const float* lse_pa
   m.splits = splits;
   m.out = static_cast<__nv_bfloat16*>(out), m.out_st = out_stride_tok, m.out_sh = out_stride_head;
   m.qsl = qsl, m.seq = seq_lens, m.n = n, m.hq = hq, m.window = window, m.block = block, m.inv_alpha = inv_alpha;
-  for (int r = 0; r < ex->world; ++r) {
-    p.recv[r] = reinterpret_cast<float*>(ex->peer[r]);
-    p.flags[r] = reinterpret_cast<uint32_t*>(ex->peer[r] + ex->off_flags);
-  }
-  p.my_recv = reinterpret_cast<const float*>(ex->base);
-  p.my_flags = reinterpret_cast<const uint32_t*>(ex->base + ex->off_flags);
+  for (int r = 0; r < ex->world; ++r) p.recv[r] = ex->peer[r];
+  p.my_recv = ex->base;
   p.ctr = reinterpret_cast<uint32_t*>(ex->base + ex->off_ctr);
-  p.part_floats = ex->part_floats, p.max_items = ex->max_items;
+  p.max_items = ex->max_items;
   p.items = static_cast<int>(items), p.slices = slices, p.hd = hd;
   p.world = ex->world, p.rank = ex->rank, p.err = err;
 
-  // Every block pushes all of its items before it waits for any, and all blocks must be resident
-  // together (a block that waits must not keep a pushing block of another rank from running):
+  // Block b of every rank handles the same items in the same order and pushes each item before it
+  // waits for the peers' records of it, so all blocks must be resident together (a block that
+  // waits must not keep the block of another rank that it waits for from running on that rank):
   // the grid is at most what the device holds at once, and the launch is cooperative.
   int per_sm = 0;
   st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exchange_merge_kernel, kMergeWarps * 32, 0),

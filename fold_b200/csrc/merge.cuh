@@ -147,15 +147,12 @@ __device__ __forceinline__ void combine_slice(const MergeParams& p, int t, int h
   lse_far = any ? mx + logf(W) : -INFINITY;
 }
 
-// The alpha-weighted merge of the window read with a combined far partial (fold/kernels.py:94-107)
-// for the 4 columns of one lane, written as bf16.
-__device__ __forceinline__ void merge_store(const MergeParams& p, int t, int h, int col, const float (&of)[4],
-                                            float lse_far) {
-  float ol[4];
-  load_row<4>(p.o_l, 1, static_cast<int64_t>(t) * p.ol_st + static_cast<int64_t>(h) * p.ol_sh + col, ol);
+// The alpha-weighted merge (fold/kernels.py:94-107) of the window read (ol, its LSE ll) with a
+// combined far partial for the 4 columns of one lane, written as bf16.
+__device__ __forceinline__ void merge_store_loaded(const MergeParams& p, int t, int h, int col, const float (&of)[4],
+                                                   float lse_far, const float (&ol)[4], float ll) {
   float y[4] = {ol[0], ol[1], ol[2], ol[3]};
   if (lse_far != -INFINITY) {
-    const float ll = p.lse_l[static_cast<int64_t>(h) * p.ll_sh + static_cast<int64_t>(t) * p.ll_st];
     const float lfa = lse_far * p.inv_alpha;  // memory log-mass (Eq. 3)
     const float m = fmaxf(ll, lfa);
     const float wl = expf(ll - m), wf = expf(lfa - m);
@@ -166,6 +163,16 @@ __device__ __forceinline__ void merge_store(const MergeParams& p, int t, int h, 
   __nv_bfloat16* o = p.out + static_cast<int64_t>(t) * p.out_st + static_cast<int64_t>(h) * p.out_sh + col;
   *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(y[0], y[1]);
   *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(y[2], y[3]);
+}
+
+// The same, loading the window read itself.
+__device__ __forceinline__ void merge_store(const MergeParams& p, int t, int h, int col, const float (&of)[4],
+                                            float lse_far) {
+  float ol[4];
+  load_row<4>(p.o_l, 1, static_cast<int64_t>(t) * p.ol_st + static_cast<int64_t>(h) * p.ol_sh + col, ol);
+  const float ll = lse_far != -INFINITY ? p.lse_l[static_cast<int64_t>(h) * p.ll_sh + static_cast<int64_t>(t) * p.ll_st]
+                                        : 0.f;
+  merge_store_loaded(p, t, h, col, of, lse_far, ol, ll);
 }
 
 }  // namespace fold

@@ -53,12 +53,23 @@ class ShardPlan:
             raise ValueError("shard chunks must be whole 256-entry pages")
         return cls(int(length), int(world), int(rank), int(chunk))
 
+    @classmethod
+    def for_far(cls, length: int, window: int, block: int, world: int, rank: int) -> "ShardPlan":
+        """Chunks that split the far keys [0, length - window - block) evenly (whole pages); the last
+        rank also holds the positions of the recent window and the block, which the far read does
+        not touch."""
+        far = max(int(length) - int(window) - int(block), 1)
+        chunk = max(SIDE_BLOCK, math.ceil(math.ceil(far / world) / SIDE_BLOCK) * SIDE_BLOCK)
+        return cls.even(length, world, rank, chunk)
+
     @property
     def pos_lo(self) -> int:
         return self.rank * self.chunk  # a rank past the end holds nothing (held == 0)
 
     @property
     def held(self) -> int:
+        if self.rank == self.world - 1:  # the last rank holds everything from its chunk start on
+            return max(0, self.length - self.pos_lo)
         return max(0, min(self.chunk, self.length - self.pos_lo))
 
     def owner(self, pos: int) -> int:

@@ -88,9 +88,13 @@ def run(world, mode, timeout=60):
     return results
 
 
-def test_shard_plan_covers_every_position_once():
+@pytest.mark.parametrize("kind", ["even", "for_far"])
+def test_shard_plan_covers_every_position_once(kind):
     for length, world in ((131072 + 2000, 8), (1500, 2), (300, 4), (262144, 3)):
-        plans = [ShardPlan.even(length, world, r) for r in range(world)]
+        if kind == "even":
+            plans = [ShardPlan.even(length, world, r) for r in range(world)]
+        else:
+            plans = [ShardPlan.for_far(length, 2048 if length > 4096 else 40, 10, world, r) for r in range(world)]
         covered = np.zeros(length, dtype=int)
         for p in plans:
             assert p.pos_lo % 256 == 0 and p.chunk % 256 == 0
@@ -99,6 +103,16 @@ def test_shard_plan_covers_every_position_once():
         for pos in (0, length // 2, length - 1):
             p = plans[plans[0].owner(pos)]
             assert p.pos_lo <= pos < p.pos_lo + p.held
+
+
+def test_far_plan_balances_the_far_keys():
+    length, W, B = 131072 + 1100, 2048, 10
+    far = length - W - B
+    for world in (2, 4, 8):
+        plans = [ShardPlan.for_far(length, W, B, world, r) for r in range(world)]
+        keys = [max(0, min(p.pos_lo + p.held, far) - p.pos_lo) for p in plans]
+        assert sum(keys) == far
+        assert max(keys) - min(keys) <= world * 256  # whole pages: the last rank takes the rest
 
 
 def test_pack_unpack_round_trip():
