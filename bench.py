@@ -457,47 +457,50 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     sharded = ShardedFarMemory(plan, ws, exchange=args.exchange) if world > 1 else None
     gen = torch.Generator().manual_seed(args.seed + 99)
     max_acc = int(acc.max())
-    h_q = torch.randn((total, B, hq, hd), generator=gen).to(torch.bfloat16).pin_memory()
-    h_k = torch.randn((total, max_acc, hkv, hd), generator=gen).to(torch.bfloat16).pin_memory()
-    h_v = torch.randn((total, max_acc, hkv, hd), generator=gen).to(torch.bfloat16).pin_memory()
-    h_pos = torch.zeros((total, max_acc), dtype=torch.int64)
+    # One pinned record per step, uploaded with one copy: the step's query, the K/V and positions
+    # of the tokens the previous step accepted, and the step's seq_len (every field 8-byte aligned).
+    qb, kb = B * hq * hd * 2, max_acc * hkv * hd * 2
+    off_k, off_v, off_pos = qb, qb + kb, qb + 2 * kb
+    off_seq = off_pos + max_acc * 8
+    rec = (off_seq + 4 + 15) // 16 * 16
+    h_in = torch.zeros((total, rec), dtype=torch.uint8)
     for i in range(total):
-        h_pos[i, : acc[i]] = torch.arange(int(H[i]), int(H[i]) + int(acc[i]))
-    h_pos = h_pos.pin_memory()
-    h_seq = torch.from_numpy((H + B).astype("int32")).reshape(total, 1).pin_memory()
+        h_in[i, :qb].view(torch.bfloat16).copy_(torch.randn(B * hq * hd, generator=gen))
+        if i > 0:
+            a = int(acc[i - 1])
+            h_in[i, off_k:off_k + a * hkv * hd * 2].view(torch.bfloat16).copy_(torch.randn(a * hkv * hd, generator=gen))
+            h_in[i, off_v:off_v + a * hkv * hd * 2].view(torch.bfloat16).copy_(torch.randn(a * hkv * hd, generator=gen))
+            h_in[i, off_pos:off_pos + a * 8].view(torch.int64).copy_(torch.arange(int(H[i - 1]), int(H[i - 1]) + a))
+        h_in[i, off_seq:off_seq + 4].view(torch.int32).fill_(int(H[i]) + B)
+    h_in = h_in.pin_memory()
     h_out = torch.empty((B, hq, hd), dtype=torch.bfloat16).pin_memory()
-    d_q = torch.empty((B, hq, hd), device=dev, dtype=torch.bfloat16)
-    d_k = torch.empty((max_acc, hkv, hd), device=dev, dtype=torch.bfloat16)
-    d_v = torch.empty_like(d_k)
-    d_pos = torch.empty(max_acc, device=dev, dtype=torch.int64)
-    d_seq = torch.empty(1, device=dev, dtype=torch.int32)
+    d_in = torch.empty(rec, device=dev, dtype=torch.uint8)
+    d_q = d_in[:qb].view(torch.bfloat16).view(B, hq, hd)
+    d_k = d_in[off_k:off_k + kb].view(torch.bfloat16).view(max_acc, hkv, hd)
+    d_v = d_in[off_v:off_v + kb].view(torch.bfloat16).view(max_acc, hkv, hd)
+    d_pos = d_in[off_pos:off_pos + max_acc * 8].view(torch.int64)
+    d_seq = d_in[off_seq:off_seq + 4].view(torch.int32)
+    accepted = {a: (d_k[:a], d_v[:a], d_pos[:a]) for a in range(1, max_acc + 1)}
     qsl = torch.tensor([0, B], dtype=torch.int32, device=dev)
     o_l = torch.randn((B, hq, hd), device=dev, dtype=torch.bfloat16)
     lse_l = torch.randn((hq, B), device=dev) + 5.0
     out = torch.empty((B, hq, hd), device=dev, dtype=torch.bfloat16)
-    h2d = d2h = 0
     from fold_b200 import kernels
+    scale = hd ** -0.5
 
     def step(i):
-        nonlocal h2d, d2h
+        d_in.copy_(h_in[i], non_blocking=True)
         a = int(acc[i - 1]) if i > 0 else 0
-        d_q.copy_(h_q[i], non_blocking=True)
-        d_seq.copy_(h_seq[i], non_blocking=True)
-        h2d_i = d_q.numel() * 2 + 4
         if a:
-            d_k[:a].copy_(h_k[i - 1, :a], non_blocking=True)
-            d_v[:a].copy_(h_v[i - 1, :a], non_blocking=True)
-            d_pos[:a].copy_(h_pos[i - 1, :a], non_blocking=True)
-            h2d_i += 2 * a * hkv * hd * 2 + a * 8
-            ws.append(d_k[:a], d_v[:a], d_pos[:a], d_pos[:a])
+            k, v, pos = accepted[a]
+            ws.append(k, v, pos, pos)
         if sharded is not None:
-            o_all, lse_all = sharded.step(d_q, qsl, d_seq, hd ** -0.5)
+            o_all, lse_all = sharded.step(d_q, qsl, d_seq, scale)
             sharded.merge(o_l, lse_l, o_all, lse_all, out, qsl, d_seq)
         else:
-            o_part, lse_part = ws.read_far(d_q, qsl, d_seq, hd ** -0.5)
+            o_part, lse_part = ws.read_far(d_q, qsl, d_seq, scale)
             kernels.merge(o_l, lse_l, o_part, lse_part, out, qsl, d_seq, window=W, block=B, alpha=ALPHA)
         h_out.copy_(out, non_blocking=True)
-        return h2d_i, out.numel() * 2
 
     for i in range(args.warmup):
         step(i)
@@ -508,9 +511,7 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for j in range(args.steps):
-        a, b = step(args.warmup + j)
-        h2d += a
-        d2h += b
+        step(args.warmup + j)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
@@ -519,8 +520,10 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     if sharded is not None and sharded.peer is not None:
         sharded.peer.close()
     return {"value": round(1000.0 * float(ms) / args.steps, 3), "unit": "us/draft-step",
-            "h2d_bytes_per_step": int(h2d / args.steps), "d2h_bytes_per_step": int(d2h / args.steps),
-            "api": "FoldWorkspace.append/read_far + kernels.merge (fold_b200 C-ABI), pinned host buffers"}
+            "h2d_bytes_per_step": rec, "d2h_bytes_per_step": out.numel() * 2,
+            "api": ("FoldWorkspace.append/read_far + " + ("ShardedFarMemory step/merge" if sharded is not None
+                                                           else "kernels.merge") + " (fold_b200 C-ABI); per step one "
+                    "pinned host->device copy of the step's inputs and one device->host copy of the output")}
 
 
 # ------------------------------------------------------------------------------ reference arm

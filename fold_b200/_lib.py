@@ -68,11 +68,17 @@ def load():
     return _lib
 
 
+_fns = {}
+
+
 def call(name: str, *args) -> None:
     """Calls an entry point and raises FoldError on a non-zero status."""
-    lib = load()
-    status = getattr(lib, name)(*args)
+    fn = _fns.get(name)
+    if fn is None:
+        fn = _fns[name] = getattr(load(), name)
+    status = fn(*args)
     if status:
+        lib = load()
         msg = lib.fold_last_error().decode(errors="replace")
         kind = lib.fold_status_string(status).decode()
         raise FoldError(f"{name}: {kind}: {msg}")

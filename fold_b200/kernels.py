@@ -23,7 +23,14 @@ def _p(t):
     return None if t is None else t.data_ptr()
 
 
+# The raw handle of the current stream without building a torch.cuda.Stream object (~0.2 us
+# instead of ~2 us per call); the public accessor where this torch build lacks it.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: torch.Tensor) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(t.get_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -156,8 +163,10 @@ def append(k, v, positions, slots, side, *, pos_lo=0, skip_foreign=False, err=No
         raise FoldError("append: K/V must be [ctx, Hkv, head_dim] matching the side cache")
     if k.stride(-1) != 1 or v.stride(-1) != 1:
         raise FoldError("append: the head dimension of K and V must be contiguous")
-    positions = positions[:ctx].to(torch.int64)
-    slots = slots[:ctx].to(torch.int64)
+    if positions.shape[0] != ctx or positions.dtype != torch.int64:
+        positions = positions[:ctx].to(torch.int64)
+    if slots.shape[0] != ctx or slots.dtype != torch.int64:
+        slots = slots[:ctx].to(torch.int64)
     _lib.call("fold_append", _p(k), k.stride(0), k.stride(1), _p(v), v.stride(0), v.stride(1), _p(positions),
               _p(slots), ctx, _p(side), pages, hkv, d2 // 2, int(pos_lo), int(bool(skip_foreign)), _p(err),
               _stream(side))
