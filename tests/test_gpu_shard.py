@@ -15,6 +15,8 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
     pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
 
+GPUS = torch.cuda.device_count()
+
 
 def free_port():
     with socket.socket() as s:
@@ -127,25 +129,28 @@ def replay(p, ws, device, sharded, steps=4, replays=6):
     return same
 
 
-@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
-def test_two_gpu_sharded_read_matches_single_gpu(exchange):
+@pytest.mark.parametrize("world,exchange", [(2, "p2p"), (2, "nccl"), (4, "p2p")])
+def test_sharded_read_matches_single_gpu(world, exchange):
+    if GPUS < world:
+        pytest.skip(f"needs {world} CUDA GPUs")
     device = torch.device("cuda", 0)
     p = inputs(device)
     want = step(p, workspace(p, device), device).numpy()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, 2, port, q, exchange)) for r in range(2)]
+    procs = [ctx.Process(target=worker, args=(r, world, port, q, exchange)) for r in range(world)]
     for pr in procs:
         pr.start()
-    res = dict((r, (s, x)) for r, s, x in (q.get(timeout=300) for _ in range(2)))
+    res = dict((r, (s, x)) for r, s, x in (q.get(timeout=300) for _ in range(world)))
     for pr in procs:
         pr.join(timeout=60)
-    for r in (0, 1):
+    for r in range(world):
         assert res[r][0] == "ok", res[r]
         out, replayed = res[r][1]
         assert np.abs(out - want).max() <= 2e-2
         if exchange == "p2p":
             assert replayed, "graph replays of the peer exchange changed the output"
-    # both ranks hold the same merged output
-    assert np.array_equal(res[0][1][0], res[1][1][0])
+    # every rank holds the same merged output
+    for r in range(1, world):
+        assert np.array_equal(res[0][1][0], res[r][1][0])
