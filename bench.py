@@ -204,9 +204,19 @@ def cpu_baseline(cfg, seed, budget_s=15.0, max_steps=50):
         if time.perf_counter() - t_all > budget_s:
             break
     us = 1e6 * statistics.mean(times)
-    return dict(value=us, unit="us/draft-step", cores=os.cpu_count() or 1, kind="port",
-                sample=f"{len(times)} whole draft steps of the {cfg['name']} workload (float64 numpy oracle: "
-                       f"far query + far read + merge, BLAS threads = {os.cpu_count()})")
+    out = dict(value=us, unit="us/draft-step", cores=os.cpu_count() or 1, kind="port",
+               sample=f"{len(times)} whole draft steps of the {cfg['name']} workload (float64 numpy oracle: "
+                      f"far query + far read + merge, BLAS threads = {os.cpu_count()})")
+    try:  # the same step on one thread (one step: it takes seconds)
+        from threadpoolctl import threadpool_limits
+
+        with threadpool_limits(limits=1):
+            t0 = time.perf_counter()
+            cpu_step_oracle(cfg, int(H[0]), q, k, v, o_l, lse_l, f)
+            out["value_1_thread"] = 1e6 * (time.perf_counter() - t0)
+    except ImportError:
+        pass
+    return out
 
 
 # ------------------------------------------------------------------------------ GPU arm
