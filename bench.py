@@ -287,11 +287,14 @@ def run_gpu(args):
         kernels.far_read(q_all[i], qsl, seq_all[i: i + 1], side, o_part, lse_part, window=W, block=B,
                          far_distance=W + B, softmax_scale=scale, table=table, pos_lo=pos_lo, capacity=length, err=err)
 
-    def step(i):
+    def append(i):
         a = int(acc[i - 1]) if i > 0 else 0
         if a:  # tokens accepted by the previous step become committed context
             kernels.append(new_k[i - 1, :a], new_v[i - 1, :a], new_pos[i - 1, :a], new_pos[i - 1, :a], side,
                            pos_lo=pos_lo, skip_foreign=world > 1, err=err)
+
+    def step(i):
+        append(i)
         seq = seq_all[i: i + 1]
         far(i)
         if peer is not None:
@@ -381,6 +384,8 @@ def run_gpu(args):
     torch.cuda.synchronize()
     far_sustained_ms = f0.elapsed_time(f1) / args.steps
     del far_graph
+    window = run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err,
+                        append) if world == 1 else None
     # every rank takes part in the reduction before any rank may raise (same collectives everywhere)
     t = torch.tensor([ms, far_ms, far_sustained_ms, float(err.item())], device=dev, dtype=torch.float64)
     if world > 1:
@@ -435,6 +440,8 @@ def run_gpu(args):
             "clocks": clocks.summary(),
             "e2e": e2e,
         }
+        if window is not None:
+            line["window_read"] = window
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, args.seed)
         print(json.dumps(line), flush=True)
@@ -443,6 +450,87 @@ def run_gpu(args):
         peer.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err, append):
+    """The window (exact-position) read, which the headline step takes as an input, measured on
+    its own (16 splits per KV head) and inside the whole draft step: append + one launch of the far
+    read (splits - 1 per KV head) beside the window read (1 per KV head) + merge of both split
+    sets. The drafter's paged cache (block size 16, shuffled blocks) holds every position a step's
+    window reaches; each split reads a contiguous part of the window [H - W - B + 1, H + B)."""
+    import numpy as np
+    import torch
+
+    from fold_b200 import kernels
+
+    hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
+    bs, wsplits = 16, 16
+    lo = max(int(H[args.warmup]) - W - B - 256, 0) // bs  # first logical block any timed step's tiles touch
+    nbl = -(-length // bs)
+    rng = np.random.default_rng(args.seed + 5)
+    table_np = np.zeros((1, nbl), dtype=np.int32)
+    table_np[0, lo:] = rng.permutation(nbl - lo)
+    block_table = torch.from_numpy(table_np).to(dev)
+    kv = torch.randn((nbl - lo, hkv, bs, 2 * hd), device=dev, dtype=torch.bfloat16)
+    kc, vc = kernels.paged_planes(kv, hd)
+    wo = torch.empty((wsplits, B, hq, hd), device=dev, dtype=torch.float32)
+    wl = torch.empty((wsplits, hq, B), device=dev, dtype=torch.float32)
+    scale = hd ** -0.5
+    fsplits = max(kernels.default_splits(hkv) - 1, 1)
+    far_parts = (torch.empty((fsplits, B, hq, hd), device=dev), torch.empty((fsplits, hq, B), device=dev))
+    win_parts = (torch.empty((1, B, hq, hd), device=dev), torch.empty((1, hq, B), device=dev))
+    ws = (W + B - 1, B - 1)
+
+    def window(i):
+        kernels.window_read(q_all[i], qsl, seq_all[i: i + 1], kc, vc, block_table, wo, wl, window_size=ws,
+                            causal=False, softmax_scale=scale, err=err)
+
+    def full_step(i):
+        append(i)
+        seq = seq_all[i: i + 1]
+        kernels.step_read(q_all[i], q_all[i], qsl, seq, side, far_parts, kc, vc, block_table, win_parts, window=W,
+                          block=B, far_distance=W + B, softmax_scale=scale, alpha=ALPHA, window_size=ws,
+                          causal=False, table=table, pos_lo=pos_lo, capacity=length, err=err)
+        kernels.merge_partials(win_parts[0], win_parts[1], far_parts[0], far_parts[1], out, qsl, seq, window=W,
+                               block=B, alpha=ALPHA)
+
+    def graph_of(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for j in range(args.steps):
+                fn(args.warmup + j)
+        g.replay()
+        torch.cuda.synchronize()
+        return g
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def time_graph(g):
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return 1000.0 * e0.elapsed_time(e1) / args.steps
+
+    wg = graph_of(window)
+    w_us = time_graph(wg)
+    del wg
+    fg = graph_of(full_step)
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 0.3:  # sustained, like the headline step
+        fg.replay()
+        torch.cuda.synchronize()
+    f_us = time_graph(fg)
+    del fg
+    keys = statistics.mean(min(W + 2 * B - 1, int(H[args.warmup + j]) + B) for j in range(args.steps))
+    alg = keys * hkv * 2 * hd * 2 + B * hq * hd * 2 + wsplits * (B * hq * hd + hq * B) * 4
+    return {"kernel": "window_read_kernel", "us": round(w_us, 3), "splits": wsplits, "block_size": bs,
+            "algorithmic_bytes": int(alg), "achieved_gbs": round(alg / (w_us * 1e-6) / 1e9, 1),
+            "timing": "burst: K window reads back to back in one graph",
+            "full_step_us": round(f_us, 3),
+            "full_step": f"append + one launch of the far read ({fsplits} splits per KV head) beside the window read "
+                         "(1 split per KV head) + merge of both split sets (no synthetic window input), one graph "
+                         "of K steps, sustained"}
 
 
 def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local):

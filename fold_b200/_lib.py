@@ -34,6 +34,13 @@ SIGNATURES = {
     "fold_merge": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp,
                    _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp],
     "fold_combine": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp],
+    "fold_window_read": [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i64, _i64, _i64, _vp, _i32, _i32, _i32,
+                         _i32, _f32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
+    "fold_step_read": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp,
+                       _vp, _i32, _vp, _vp, _i64, _i32, _i64, _i64, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _i32,
+                       _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _vp, _vp],
+    "fold_merge_partials": [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+                            _f32, _vp],
     "fold_exchange_create": [_i32, _i32, _i64, _i32, ctypes.POINTER(ctypes.c_void_p), _vp],
     "fold_exchange_open": [_vp, _vp],
     "fold_exchange_destroy": [_vp],

@@ -9,10 +9,13 @@ local_splits), the same side-cache tensor and report. What changes is the work b
     writes split partials, instead of far_query plus a FlashAttention call over the side cache;
   * the merge combines those partials with the window read in one kernel (kernels.merge);
   * the side-cache append is one 16-byte-vector kernel per layer (kernels.append), issued before
-    the keys are rotated, so no copy of the un-rotated keys is needed.
+    the keys are rotated, so no copy of the un-rotated keys is needed;
+  * the window (exact-position) read of the drafter's paged cache is the same split-read kernel in
+    its paged mode (kernels.window_read), instead of a FlashAttention call; the merge combines its
+    split partials with the far read's (kernels.merge_partials).
 
-The window (exact-position) read still calls FlashAttention through vLLM, as the reference does;
-FoldAttention takes another `local_read` callable for tests or other backends.
+No FlashAttention call is left on the step. A layer may still be given a `local_read` callable
+returning (o, lse) in FlashAttention's layout, which then replaces the window read.
 
 Geometry of a draft step with block B at positions H .. H+B-1 (H = seq_len - qlen): context
 entries with p - j < D = W + B are read at their true distances by the window read; older ones
@@ -85,8 +88,16 @@ class FoldWorkspace:
         self.far_splits = int(splits) if splits else None
         self._table = None
         self._parts = {}
-        if num_heads is not None and mode != "window":
-            self.partials(self.block, int(num_heads))
+        self._window_parts = {}
+        self._step_far, self._step_window = {}, {}
+        if num_heads is not None:  # the buffers the forward of this layer uses, before any graph capture
+            if mode == "window" or self.sharded:
+                self.window_partials(self.block, int(num_heads))
+            if mode != "window":
+                if self.sharded:
+                    self.partials(self.block, int(num_heads))
+                else:
+                    self.step_partials(self.block, int(num_heads))
 
     # -- derived state ---------------------------------------------------------------------------
     @property
@@ -118,6 +129,17 @@ class FoldWorkspace:
             self._parts[key] = buf
         return buf
 
+    def window_partials(self, n: int, num_heads: int):
+        """Split partial buffers of the window read (local_splits splits) for n rows."""
+        return _partial_buffers(self._window_parts, self.local_splits, n, num_heads, self.head_dim, self.device)
+
+    def step_partials(self, n: int, num_heads: int):
+        """(far, window) split buffers of the one-launch step read: splits() - 1 far splits beside
+        one window split per KV head, so that the launch stays one wave of CTAs."""
+        far = _partial_buffers(self._step_far, max(self.splits() - 1, 1), n, num_heads, self.head_dim, self.device)
+        win = _partial_buffers(self._step_window, 1, n, num_heads, self.head_dim, self.device)
+        return far, win
+
     def check(self) -> None:
         """Raises FoldError if a kernel recorded a device-side error (synchronises)."""
         word = int(self.err.item())
@@ -141,6 +163,31 @@ class FoldWorkspace:
                          capacity=self.capacity, err=self.err)
         return o_part, lse_part
 
+    def read_step(self, q, q_window, qsl, seq_lens, scale, kv_cache, block_table, *, window_size, causal,
+                  rotate=True):
+        """The far read of q (rotated, as read_far) and the window read of q_window over the
+        drafter's paged cache kv_cache [blocks, Hkv, block_size, 2D] in one launch. Returns the
+        (far, window) split partials, for kernels.merge_partials."""
+        n, hq, _ = q.shape
+        far, win = self.step_partials(n, hq)
+        k, v = kernels.paged_planes(kv_cache, self.head_dim)
+        kernels.step_read(q, q_window, qsl, seq_lens, self.side, far, k, v, block_table, win, window=self.window,
+                          block=self.block, far_distance=self.far_distance, softmax_scale=scale, alpha=self.alpha,
+                          window_size=window_size, causal=causal, table=self.table if rotate else None,
+                          far_len=self.far_len, pos_lo=self.pos_lo, capacity=self.capacity, err=self.err)
+        return far, win
+
+
+def _partial_buffers(cache: dict, splits: int, n: int, num_heads: int, head_dim: int, device):
+    """(o [splits, n, Hq, D], lse [splits, Hq, n]) float32, allocated once per shape."""
+    key = (int(splits), int(n), int(num_heads))
+    buf = cache.get(key)
+    if buf is None:
+        buf = (torch.empty((splits, n, num_heads, head_dim), device=device, dtype=torch.float32),
+               torch.empty((splits, num_heads, n), device=device, dtype=torch.float32))
+        cache[key] = buf
+    return buf
+
 
 def logn_scale_rows(q, query_start_loc, seq_lens, logn_ref):
     """ReRoPE query scale max(1, log(p + 1) / log(ref)) at the absolute position p of each row
@@ -153,25 +200,13 @@ def logn_scale_rows(q, query_start_loc, seq_lens, logn_ref):
     return (q.float() * s[:, None, None]).to(q.dtype)
 
 
-def _flash_local_read(query, kv_cache, meta, original, *, window_size, causal, num_splits):
-    """Exact-position read through vLLM's FlashAttention (the reference's window read)."""
-    from vllm.vllm_flash_attn import flash_attn_varlen_func
-
-    nk, nv = kv_cache.transpose(1, 2).split(original.head_size, dim=-1)
-    return flash_attn_varlen_func(
-        q=query, k=nk, v=nv, cu_seqlens_q=meta.query_start_loc, max_seqlen_q=meta.max_query_len,
-        seqused_k=meta.seq_lens, max_seqlen_k=meta.max_seq_len, softmax_scale=original.scale, causal=causal,
-        window_size=list(window_size), block_table=meta.block_table, return_softmax_lse=True,
-        fa_version=original.vllm_flash_attn_version, num_splits=num_splits)
-
-
 LocalRead = Callable[..., Any]
 
 
 class _Wrapped:
     def __init__(self, original: Any, local_read: Optional[LocalRead] = None):
         self.original = original
-        self.local_read = local_read or _flash_local_read
+        self.local_read = local_read
 
     def __getattr__(self, name):
         return getattr(self.original, name)
@@ -185,13 +220,73 @@ class _Wrapped:
         if meta.use_cascade or not isinstance(meta.causal, bool):
             raise FoldError("cascade attention and dynamic causality are not supported")
 
+    def _fold_read(self, w, q_far, q_win, kv_cache, meta, out, *, window_size, causal, num_splits, rotate):
+        """Far read + window read + merge of a FOLD layer into out [n, Hq, D]: one launch for both
+        reads when the window read is this package's and the side cache is not sharded."""
+        o, qsl, seq = self.original, meta.query_start_loc, meta.seq_lens
+        local = dict(window_size=window_size, causal=causal, num_splits=num_splits, window=w.window,
+                     block=w.block, alpha=w.alpha, err=w.err)
+        if self.local_read is None and not w.sharded:
+            far, win = w.read_step(q_far, q_win, qsl, seq, o.scale, kv_cache, meta.block_table,
+                                   window_size=window_size, causal=causal, rotate=rotate)
+            kernels.merge_partials(win[0], win[1], far[0], far[1], out, qsl, seq, window=w.window, block=w.block,
+                                   alpha=w.alpha)
+            return
+        if rotate:
+            far = w.read_far(q_far, qsl, seq, o.scale)
+        else:
+            far = w.read_far(q_far, qsl, seq, o.scale, rotate=False)
+        parts = None if self.local_read is not None else w.window_partials(out.shape[0], out.shape[1])
+        self._window_and_merge(q_win, kv_cache, meta, parts, far, out, **local)
+
+    def _window_and_merge(self, q, kv_cache, meta, parts, far, out, *, window_size, causal, num_splits, window,
+                          block, alpha, err):
+        """The window read of q over the layer's paged cache, merged with the far partials `far`
+        ((o, lse) or None) into out [n, Hq, D]. `parts` are the window read's split buffers."""
+        o = self.original
+        qsl, seq = meta.query_start_loc, meta.seq_lens
+        if self.local_read is not None:
+            out_l, lse_l = self.local_read(q, kv_cache, meta, o, window_size=window_size, causal=causal,
+                                           num_splits=num_splits)
+            if far is None:
+                out.copy_(out_l.reshape(out.shape))
+            else:
+                kernels.merge(out_l.view(out.shape), lse_l, far[0], far[1], out, qsl, seq, window=window,
+                              block=block, alpha=alpha)
+            return
+        k, v = kernels.paged_planes(kv_cache, o.head_size)
+        kernels.window_read(q, qsl, seq, k, v, meta.block_table, parts[0], parts[1], window_size=window_size,
+                            causal=causal, softmax_scale=o.scale, err=err)
+        kernels.merge_partials(parts[0], parts[1], None if far is None else far[0], None if far is None else far[1],
+                               out, qsl, seq, window=window, block=block, alpha=alpha)
+
 
 class NativeWindowAttention(_Wrapped):
-    """Native sliding-window read, optionally with the ReRoPE query scale."""
+    """Native sliding-window read, optionally with the ReRoPE query scale (fold/attention.py:98-123):
+    the window read kernel over the layer's own window, its splits combined into the output."""
 
-    def __init__(self, original: Any, logn_ref: int = 0, local_read: Optional[LocalRead] = None):
+    splits = 16  # num_splits of the reference's read (fold/attention.py:121)
+
+    def __init__(self, original: Any, logn_ref: int = 0, local_read: Optional[LocalRead] = None,
+                 block: Optional[int] = None, device=None):
         super().__init__(original, local_read)
         self.logn_ref = int(logn_ref)
+        self._parts = {}
+        self.err = None
+        if block is not None and device is not None and local_read is None:
+            self._buffers(int(block), int(original.num_heads), device)  # before any graph capture
+
+    def _buffers(self, n, hq, device):
+        if self.err is None:
+            self.err = torch.zeros(1, device=device, dtype=torch.int32)
+        return _partial_buffers(self._parts, self.splits, n, hq, self.original.head_size, device)
+
+    def check(self) -> None:
+        """Raises FoldError if the window read recorded a device-side error (synchronises)."""
+        if self.err is not None and int(self.err.item()):
+            word = int(self.err.item())
+            self.err.zero_()
+            raise FoldError(f"FOLD device error: {describe_device_error(word)}")
 
     def forward(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale=None,
                 output_block_scale=None):
@@ -205,9 +300,11 @@ class NativeWindowAttention(_Wrapped):
         q = query[:n]
         if self.logn_ref:
             q = logn_scale_rows(q, meta.query_start_loc, meta.seq_lens, self.logn_ref)
-        out, _ = self.local_read(q, kv_cache, meta, o, window_size=o.sliding_window, causal=meta.causal,
-                                 num_splits=16)
-        output[:n].copy_(out.reshape(output[:n].shape))
+        hq = q.shape[1]
+        parts = None if self.local_read is not None else self._buffers(n, hq, q.device)
+        self._window_and_merge(q, kv_cache, meta, parts, None, output[:n].view(n, hq, o.head_size),
+                               window_size=o.sliding_window, causal=meta.causal, num_splits=self.splits, window=1,
+                               block=1, alpha=1.0, err=self.err)
         return output
 
 
@@ -231,23 +328,25 @@ class FoldAttention(_Wrapped):
         B = w.block
         qsl, seq = meta.query_start_loc, meta.seq_lens
         q = query[:n]
-        local = dict(window_size=(w.window + B - 1, B - 1), causal=False, num_splits=w.local_splits)
+        hq = q.shape[1]
+        out = output[:n].view(n, hq, o.head_size)
+        # the window read: non-causal, window [W + B - 1, B - 1] (fold/attention.py:148-151)
+        window_size = (w.window + B - 1, B - 1)
         if w.mode == "window":
-            out_l, _ = self.local_read(q, kv_cache, meta, o, **local)
-            output[:n].copy_(out_l.reshape(output[:n].shape))
+            parts = None if self.local_read is not None else w.window_partials(n, hq)
+            self._window_and_merge(q, kv_cache, meta, parts, None, out, window_size=window_size, causal=False,
+                                   num_splits=w.local_splits, window=w.window, block=B, alpha=w.alpha, err=w.err)
             return output
         if q.stride(-1) != 1:
             q = q.contiguous()
+        q_far, rotate = q, True
         if w.mode == "rerope":
-            q, qf = kernels.rerope_queries(q, qsl, seq, w.inv_freq, w.far_len, far_distance=w.far_distance,
-                                           window=w.window, block=B, constant=True, logn_ref=w.logn_ref,
-                                           table=w.table)
-            o_part, lse_part = w.read_far(qf, qsl, seq, o.scale, rotate=False)
-        else:
-            o_part, lse_part = w.read_far(q, qsl, seq, o.scale)
-        out_l, lse_l = self.local_read(q, kv_cache, meta, o, **local)
-        kernels.merge(out_l.view(n, -1, o.head_size), lse_l, o_part, lse_part, output[:n].view(n, -1, o.head_size),
-                      qsl, seq, window=w.window, block=B, alpha=w.alpha)
+            q, q_far = kernels.rerope_queries(q, qsl, seq, w.inv_freq, w.far_len, far_distance=w.far_distance,
+                                              window=w.window, block=B, constant=True, logn_ref=w.logn_ref,
+                                              table=w.table)
+            rotate = False
+        self._fold_read(w, q_far, q, kv_cache, meta, out, window_size=window_size, causal=False,
+                        num_splits=w.local_splits, rotate=rotate)
         return output
 
 
@@ -276,16 +375,15 @@ class SlidingFoldAttention(_Wrapped):
         B = w.block
         qn = logn_scale_rows(query[:n], qsl, seq, w.logn_ref) if w.logn_ref else query[:n]
         qp = qn if qn.stride(-1) == 1 else qn.contiguous()
+        q_far, rotate = qp, True
         if w.mode == "rerope":
-            _, qf = kernels.rerope_queries(qp, qsl, seq, w.inv_freq, w.far_len, far_distance=w.far_distance,
-                                           window=w.window, block=B, constant=True, logn_ref=0, table=w.table)
-            o_part, lse_part = w.read_far(qf, qsl, seq, o.scale, rotate=False)
-        else:
-            o_part, lse_part = w.read_far(qp, qsl, seq, o.scale)
-        out_l, lse_l = self.local_read(qn, kv_cache, meta, o, window_size=o.sliding_window, causal=meta.causal,
-                                       num_splits=16)
-        kernels.merge(out_l.view(n, -1, o.head_size), lse_l, o_part, lse_part, output[:n].view(n, -1, o.head_size),
-                      qsl, seq, window=w.window, block=B, alpha=w.alpha)
+            _, q_far = kernels.rerope_queries(qp, qsl, seq, w.inv_freq, w.far_len, far_distance=w.far_distance,
+                                              window=w.window, block=B, constant=True, logn_ref=0, table=w.table)
+            rotate = False
+        hq = qn.shape[1]
+        # the native causal sliding read is the local branch (fold/attention.py:211-215)
+        self._fold_read(w, q_far, qn, kv_cache, meta, output[:n].view(n, hq, o.head_size),
+                        window_size=o.sliding_window, causal=meta.causal, num_splits=w.local_splits, rotate=rotate)
         return output
 
 
@@ -387,7 +485,8 @@ def install(speculator: Any, *, window: int, alpha: float = 2.0, mode: str = "fo
                     read the memory as well
     logn_ref        reference length of the ReRoPE query scale (rerope mode)
     local_splits    split count of the window read
-    local_read      optional replacement of the FlashAttention window read (tests, other backends)
+    local_read      optional replacement of the window read: a callable returning (o, lse) in
+                    FlashAttention's layout
     """
     previous = getattr(speculator, "_fold_installation", None)
     if previous is not None:
@@ -424,6 +523,7 @@ def install(speculator: Any, *, window: int, alpha: float = 2.0, mode: str = "fo
         layer = context[name]
         impl = layer.impl
         if local_read is None and (not _is_flash_attention(impl) or impl.vllm_flash_attn_version not in (3, 4)):
+            # the window read takes FlashAttention's paged cache layout and metadata
             raise FoldError(f"{name}: FlashAttention 3 or 4 is required")
         native = int(impl.sliding_window[0])
         if native >= 0:
@@ -438,7 +538,8 @@ def install(speculator: Any, *, window: int, alpha: float = 2.0, mode: str = "fo
                 report["fold_layers"].append(name)
                 report["side_cache_bytes"] += ws.side.numel() * ws.side.element_size()
             else:
-                layer.impl = NativeWindowAttention(impl, logn_ref, local_read)
+                layer.impl = NativeWindowAttention(impl, logn_ref, local_read, block=B,
+                                                   device=layer.kv_cache.device)
                 report["native_window_layers"].append(name)
             continue
         ws = make_workspace(layer, dl, window)

@@ -81,6 +81,44 @@ __device__ __forceinline__ void issue_tile(unsigned char* smem, uint64_t* full, 
   for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
 }
 
+// Window read: issues the copies of the tile of positions [tpos, tpos + TK) of head h from the
+// paged cache into stage `st`, in 16-position chunks (every block size is a multiple of 16, so a
+// chunk never straddles two blocks). Each chunk lands where a TK-row box would have put it, so
+// the stage has the far read's layout. Chunks past the last context entry reload the last valid
+// chunk (the consumers zero those V rows and mask those keys); a block-table entry outside the
+// cache records FOLD_DEVERR_BLOCK_TABLE and reads block 0 instead.
+template <class C>
+__device__ __forceinline__ void issue_window_tile(unsigned char* smem, uint64_t* full, const CUtensorMap* kmap,
+                                                  const CUtensorMap* vmap, int st, int64_t tpos, int seq, int h,
+                                                  const FarParams& p, uint64_t pol) {
+  constexpr int CH = C::TK / 16;
+  const int64_t last = (static_cast<int64_t>(seq - 1) / 16) * 16;  // a tile exists only when seq >= 1
+  int blk[CH], slot[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {  // all table loads first: one latency for the whole tile
+    const int64_t pos = min64(tpos + 16 * c, last);
+    const int lb = static_cast<int>(pos / p.block_size);
+    slot[c] = static_cast<int>(pos - static_cast<int64_t>(lb) * p.block_size);
+    blk[c] = lb < p.bt_len ? __ldg(p.block_table + lb) : -1;
+  }
+  mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+  unsigned char* dst = smem + st * C::STAGE_BYTES;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    int b = blk[c];
+    if (b < 0 || b >= p.num_blocks) {
+      set_error(p.err, FOLD_DEVERR_BLOCK_TABLE);
+      b = 0;
+    }
+    const int c1 = p.head_inner ? h : slot[c], c2 = p.head_inner ? slot[c] : h;
+#pragma unroll
+    for (int x = 0; x < C::KBOX; ++x) {
+      tma_load_4d(dst + x * C::BOX_BYTES + c * 2048, kmap, &full[st], x * 64, c1, c2, b, pol);
+      tma_load_4d(dst + (C::KBOX + x) * C::BOX_BYTES + c * 2048, vmap, &full[st], x * 64, c1, c2, b, pol);
+    }
+  }
+}
+
 // Vectorised far-query rotation: each work item is one row's pair of 8-element chunks
 // ([8c, 8c+8) with its neox partner [RH+8c, ...), or 16 unrotated elements), loaded as 16-byte
 // vectors. Every thread issues the loads of all its items before any arithmetic, so the prologue
@@ -156,9 +194,41 @@ __device__ __forceinline__ void rotate_query_vec(const FarParams& p, const float
   }
 }
 
+// Window read: first and one-past-last visible position of row r (at position hist + r) under the
+// FlashAttention window [p - left, p + right] (a negative side is unbounded), causal or not,
+// within the seq context entries. Both grow with r.
+__device__ __forceinline__ int64_t window_lo(const FarParams& p, int hist, int r) {
+  return p.win_left < 0 ? 0 : max64(0, static_cast<int64_t>(hist) + r - p.win_left);
+}
+__device__ __forceinline__ int64_t window_hi(const FarParams& p, int hist, int seq, int r) {
+  const int64_t pos = static_cast<int64_t>(hist) + r;
+  int64_t hi = seq;
+  if (p.win_right >= 0) hi = min64(hi, pos + p.win_right + 1);
+  if (p.causal) hi = min64(hi, pos + 1);
+  return max64(hi, 0);
+}
+
+// Zeroes the V rows [from, TK) of a landed stage (window read: positions past the context, whose
+// cache slots may hold anything; their P is 0, but 0 * NaN would not be).
 template <class C>
-__global__ void __launch_bounds__(C::NTHREADS, 1)
-    far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
+__device__ __forceinline__ void zero_v_rows(unsigned char* stage, int from) {
+  const int per_box = (C::TK - from) * 8;  // 16-byte units
+  for (int u = threadIdx.x; u < per_box * C::KBOX; u += C::NTHREADS) {
+    const int x = u / per_box, r = u - x * per_box;
+    *reinterpret_cast<uint4*>(stage + (C::KBOX + x) * C::BOX_BYTES + (from + (r >> 3)) * 128 + (r & 7) * 16) =
+        make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_shared();  // the stage is refilled by TMA later
+}
+
+// The split-KV read of one (split, KV head), in two modes.
+//   WIN = false, far memory: K|V rows of the side cache through `map`, the query rotated to the
+//     shared far position, row r reads positions [0, H - W - B + 1 + r) (fold/attention.py:164).
+//   WIN = true, window read: K through `map` and V through `vmap` from the paged cache, the
+//     query as given, row r reads its exact-position window (fold/attention.py:148-151,163).
+template <class C, bool WIN>
+__device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
+                                           int split) {
   constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
   constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
   extern __shared__ unsigned char smem_raw[];
@@ -171,48 +241,76 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   float* row_inv = row_m + 64;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int split = blockIdx.x, h = blockIdx.y;
+  const int h = blockIdx.y;
 
   // Step geometry, from the device-side lengths (fold/kernels.py:24-30).
   const int qlen = p.qsl[1] - p.qsl[0];
-  const int hist = max(p.seq[0] - qlen, 0);
-  const int far_len = max(hist - p.window - p.block + qlen, 0);
-  const int lim_base = hist - p.window - p.block + 1;  // row r reads positions [0, lim_base + r)
-  const int64_t end = min64(max(lim_base + p.n - 1, 0), p.pos_lo + p.local_cap);
-  const int64_t len = max64(end - p.pos_lo, 0);
-  const int tiles = static_cast<int>((len + TK - 1) / TK);
+  const int seq = p.seq[0];
+  const int hist = max(seq - qlen, 0);
+  int lim_base = 0;  // far: row r reads positions [0, lim_base + r)
+  int64_t end;       // far: end of this cache's keys for the last row
+  int64_t pos0;      // position of tile 0
+  int tiles;
+  if constexpr (!WIN) {
+    lim_base = hist - p.window - p.block + 1;
+    end = min64(max(lim_base + p.n - 1, 0), p.pos_lo + p.local_cap);
+    const int64_t len = max64(end - p.pos_lo, 0);
+    tiles = static_cast<int>((len + TK - 1) / TK);
+    pos0 = p.pos_lo;
+  } else {
+    const int64_t u_lo = window_lo(p, hist, 0), u_hi = window_hi(p, hist, seq, p.n - 1);
+    const int64_t t0 = u_lo / TK;
+    tiles = u_hi > u_lo ? static_cast<int>((u_hi + TK - 1) / TK - t0) : 0;
+    pos0 = t0 * TK;
+    end = u_hi;
+  }
   const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / p.splits);
   const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / p.splits) - t_begin;
 
   uint64_t pol = 0;
+  auto issue = [&](int st, int t) {  // tile t of this cache into stage st
+    if constexpr (WIN)
+      issue_window_tile<C>(smem, full, map, vmap, st, pos0 + static_cast<int64_t>(t) * TK, seq, h, p, pol);
+    else
+      issue_tile<C>(smem, full, map, st, t, p.hkv, h, pol);
+  };
   if (tid == 0) {
-    if (split == 0 && h == 0) {
-      if (p.far_len) *p.far_len = far_len;
-      if (far_len > p.capacity) set_error(p.err, FOLD_DEVERR_CAPACITY);
+    if constexpr (!WIN) {
+      if (split == 0 && h == 0) {
+        const int far_len = max(hist - p.window - p.block + qlen, 0);
+        if (p.far_len) *p.far_len = far_len;
+        if (far_len > p.capacity) set_error(p.err, FOLD_DEVERR_CAPACITY);
+      }
     }
 #pragma unroll
     for (int i = 0; i < NSTAGE; ++i) mbar_init(&full[i], 1);
     fence_mbar_init();
     // Fill the ring right away, so the first copies overlap the query rotation below.
     pol = l2_evict_first_policy();
-    prefetch_tensormap(&map);
-    for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue_tile<C>(smem, full, &map, i, t_begin + i, p.hkv, h, pol);
+    prefetch_tensormap(map);
+    if constexpr (WIN) prefetch_tensormap(vmap);
+    for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
   }
 
   const int G = p.group;
   const int nrows = p.n * G;
 
   // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table.
+  // The window read takes the query as it is.
   {
-    const int delta = p.far_distance - hist;
-    int ad = delta < 0 ? -delta : delta;
-    const float sgn = delta < 0 ? -1.f : 1.f;
-    if (p.table && ad >= p.table_rows) {
-      if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
-      ad = p.table_rows - 1;
-    }
+    const float* trow = nullptr;
+    float sgn = 1.f;
     const int RH = p.rot_dim >> 1;
-    const float* trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
+    if constexpr (!WIN) {
+      const int delta = p.far_distance - hist;
+      int ad = delta < 0 ? -delta : delta;
+      sgn = delta < 0 ? -1.f : 1.f;
+      if (p.table && ad >= p.table_rows) {
+        if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
+        ad = p.table_rows - 1;
+      }
+      trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
+    }
     if (p.vec_rot) {
       rotate_query_vec<C>(p, trow, RH, sgn, h, split, nrows, G, Qs);
     } else {
@@ -263,14 +361,22 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     }
   }
 
-  // Row limits of this thread's QK rows (global positions; 0 for padding rows).
+  // Row limits of this thread's QK rows (global positions; 0 for padding rows): keys
+  // [llo, lim) are visible, llo being 0 for the far read.
   int lim[QNT][2];
+  int llo[WIN ? QNT : 1][2];
 #pragma unroll
   for (int j = 0; j < QNT; ++j)
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const int rho = (nt_lo + j) * 8 + t4 * 2 + c;
-      lim[j][c] = (rho < nrows && nt_lo + j < NT) ? static_cast<int>(min64(lim_base + rho / G, end)) : 0;
+      const bool valid = rho < nrows && nt_lo + j < NT;
+      if constexpr (WIN) {
+        lim[j][c] = valid ? static_cast<int>(window_hi(p, hist, seq, rho / G)) : 0;
+        llo[j][c] = valid ? static_cast<int>(window_lo(p, hist, rho / G)) : 0;
+      } else {
+        lim[j][c] = valid ? static_cast<int>(min64(lim_base + rho / G, end)) : 0;
+      }
     }
 
   float oacc[PV_MT][NT][4];
@@ -301,7 +407,12 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     const bool ok = mbar_wait(&full[st], (it / NSTAGE) & 1);
     const uint32_t kv_base = smem_u32(smem + st * C::STAGE_BYTES);
     const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
-    const int64_t key0 = p.pos_lo + static_cast<int64_t>(t_begin + it) * TK + mt * 16 + g4;
+    const int64_t tpos = pos0 + static_cast<int64_t>(t_begin + it) * TK;  // first position of the tile
+    const int64_t key0 = tpos + mt * 16 + g4;
+    if constexpr (WIN) {
+      const int valid = static_cast<int>(max64(0, min64(TK, seq - tpos)));
+      if (ok && valid < TK) zero_v_rows<C>(smem + st * C::STAGE_BYTES, valid);
+    }
 
     float x[QNT][4];
     float ls[QNT][2];
@@ -340,7 +451,9 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
         for (int e = 0; e < 4; ++e) {
           const int c = e & 1;
           const int64_t key = key0 + (e >> 1) * 8;
-          const float v = key < lim[j][c] ? x[j][e] * p.scale_log2 : -INFINITY;
+          bool vis = key < lim[j][c];
+          if constexpr (WIN) vis = vis && key >= llo[j][c];
+          const float v = vis ? x[j][e] * p.scale_log2 : -INFINITY;
           x[j][e] = v;
           exceed |= v > MQ(j, c) + kRaise;
         }
@@ -371,7 +484,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
     const bool attention = named_bar_or(exceed || !ok, 1, NTH);
     if (tid == 0 && it >= 1 && it - 1 + NSTAGE < ntiles)
-      issue_tile<C>(smem, full, &map, (it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE, p.hkv, h, pol);
+      issue((it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE);
     if (attention) {
       if (named_bar_or(!ok, 2, NTH)) {
         timed_out = true;
@@ -553,6 +666,33 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   }
 }
 
+template <class C>
+__global__ void __launch_bounds__(C::NTHREADS, 1)
+    far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
+  split_read<C, false>(&map, nullptr, p, blockIdx.x);
+}
+
+template <class C>
+__global__ void __launch_bounds__(C::NTHREADS, 1)
+    window_read_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       const FarParams p) {
+  split_read<C, true>(&kmap, &vmap, p, blockIdx.x);
+}
+
+// The far read and the window read of one draft step in one launch: per KV head, the first
+// win.splits CTAs read the window, the next far.splits the far memory. A window read is a few MB
+// and runs on its own SMs while the far read streams the side cache, so it adds no time to the
+// step when the grid fits the device in one wave.
+template <class C>
+__global__ void __launch_bounds__(C::NTHREADS, 1)
+    step_read_kernel(const __grid_constant__ CUtensorMap far_map, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap, const FarParams far, const FarParams win) {
+  if (static_cast<int>(blockIdx.x) < win.splits)
+    split_read<C, true>(&kmap, &vmap, win, blockIdx.x);
+  else
+    split_read<C, false>(&far_map, nullptr, far, blockIdx.x - win.splits);
+}
+
 // ------------------------------------------------------------------ host side
 namespace {
 // -2: not read yet; -1: choose per shape; 0: mma.sync; 1: tcgen05.
@@ -588,74 +728,13 @@ static int vec_rotation_ok(const void* q, int64_t q_st, int64_t q_sh, const void
   return 1;
 }
 
-template <class C>
-int launch_far(const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
-  CUtensorMap map;
-  if (int s = side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)) return s;
-  auto kern = far_read_kernel<C>;
-  static bool configured = false;  // per instantiation
-  if (!configured) {
-    if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                           "cudaFuncSetAttribute(far_read)"))
-      return s;
-    configured = true;
-  }
-  dim3 grid(prm.splits, prm.hkv);
-  kern<<<grid, C::NTHREADS, C::SMEM, stream>>>(map, prm);
-  return check_launch("far_read_kernel");
-}
-
-template <int HD, int TK, int HG>
-int dispatch_nt(int nt, const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
-  switch (nt) {
-    case 1: return launch_far<FarCfg<HD, 1, TK, HG>>(prm, side, pages, stream);
-    case 2: return launch_far<FarCfg<HD, 2, TK, HG>>(prm, side, pages, stream);
-    case 3: return launch_far<FarCfg<HD, 3, TK, HG>>(prm, side, pages, stream);
-    case 4: return launch_far<FarCfg<HD, 4, TK, HG>>(prm, side, pages, stream);
-    case 5: return launch_far<FarCfg<HD, 5, TK, HG>>(prm, side, pages, stream);
-    case 6: return launch_far<FarCfg<HD, 6, TK, HG>>(prm, side, pages, stream);
-    case 7: return launch_far<FarCfg<HD, 7, TK, HG>>(prm, side, pages, stream);
-    case 8: return launch_far<FarCfg<HD, 8, TK, HG>>(prm, side, pages, stream);
-    default: return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
-  }
-}
-
-template <class C>
-int launch_far_uncached(const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
-  CUtensorMap map;
-  if (int s = side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map)) return s;
-  auto kern = far_read_kernel<C>;
-  static bool configured = false;  // per instantiation
-  if (!configured) {
-    if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                           "cudaFuncSetAttribute(far_read)"))
-      return s;
-    configured = true;
-  }
-  kern<<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
-  return check_launch("far_read_kernel");
-}
-
-template <int HD, int TK, int HG>
-int dispatch_nt_uncached(int nt, const FarParams& prm, const void* side, int pages, cudaStream_t stream) {
-  switch (nt) {
-    case 1: return launch_far_uncached<FarCfg<HD, 1, TK, HG>>(prm, side, pages, stream);
-    case 2: return launch_far_uncached<FarCfg<HD, 2, TK, HG>>(prm, side, pages, stream);
-    case 3: return launch_far_uncached<FarCfg<HD, 3, TK, HG>>(prm, side, pages, stream);
-    case 4: return launch_far_uncached<FarCfg<HD, 4, TK, HG>>(prm, side, pages, stream);
-    case 5: return launch_far_uncached<FarCfg<HD, 5, TK, HG>>(prm, side, pages, stream);
-    case 6: return launch_far_uncached<FarCfg<HD, 6, TK, HG>>(prm, side, pages, stream);
-    case 7: return launch_far_uncached<FarCfg<HD, 7, TK, HG>>(prm, side, pages, stream);
-    case 8: return launch_far_uncached<FarCfg<HD, 8, TK, HG>>(prm, side, pages, stream);
-    default: return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
-  }
-}
-
-int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
-                      const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side,
-                      int pages, int64_t pos_lo, int64_t capacity, int* far_len, float* o_part, float* lse_part,
-                      int splits, int n, int hq, int hkv, int hd, int window, int block, int far_distance,
-                      float softmax_scale, int* err, cudaStream_t stream) {
+// Checks the arguments of a far read (those of fold_far_read) and fills its parameter block.
+static int make_far_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                           const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side,
+                           int pages, int64_t pos_lo, int64_t capacity, int* far_len, void* qf, int64_t qf_stride_tok,
+                           int64_t qf_stride_head, float* o_part, float* lse_part, int splits, int n, int hq, int hkv,
+                           int hd, int window, int block, int far_distance, float softmax_scale, int* err,
+                           FarParams* out) {
   if (!q || !qsl || !seq_lens || !side || !o_part || !lse_part)
     return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: null pointer");
   if (n < 1 || hq < 1 || hkv < 1 || hq % hkv || splits < 1 || pages < 2 || window < 1 || block < 1)
@@ -667,8 +746,7 @@ int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   if (pos_lo < 0 || pos_lo % 256) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: pos_lo must be a multiple of 256");
   if (static_cast<int64_t>(pages) * hkv > (1ll << 31) - 1)
     return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: side cache too large for one descriptor");
-  const int rows = n * (hq / hkv);
-  if (rows > 64) return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
+  if (n * (hq / hkv) > 64) return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
   FarParams prm{};
   prm.q = static_cast<const __nv_bfloat16*>(q);
   prm.q_st = q_stride_tok, prm.q_sh = q_stride_head;
@@ -676,17 +754,163 @@ int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   prm.table = rope_table, prm.table_rows = table_rows, prm.rot_dim = rot_dim;
   prm.pos_lo = pos_lo, prm.capacity = capacity, prm.local_cap = static_cast<int64_t>(pages - 1) * 256;
   prm.far_len = far_len;
+  prm.qf = static_cast<__nv_bfloat16*>(qf), prm.qf_st = qf_stride_tok, prm.qf_sh = qf_stride_head;
   prm.o_part = o_part, prm.lse_part = lse_part;
   prm.splits = splits, prm.n = n, prm.hq = hq, prm.hkv = hkv, prm.group = hq / hkv;
   prm.window = window, prm.block = block, prm.far_distance = far_distance;
   prm.scale_log2 = softmax_scale * kLog2e;
   prm.err = err;
-  prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, nullptr, 0, 0, rope_table, rot_dim, hd);
+  prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, qf, qf_stride_tok, qf_stride_head, rope_table,
+                                rot_dim, hd);
+  *out = prm;
+  return FOLD_OK;
+}
+
+// Checks the arguments of a window read (those of fold_window_read), fills its parameter block and
+// the TMA descriptors of the K and V planes.
+static int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                              const int* seq_lens, const void* k_cache, const void* v_cache, int64_t num_blocks,
+                              int block_size, int64_t cache_stride_block, int64_t cache_stride_head,
+                              int64_t cache_stride_slot, const int* block_table, int block_table_len,
+                              int window_left, int window_right, int causal, float softmax_scale, float* o_part,
+                              float* lse_part, int splits, int n, int hq, int hkv, int hd, int* err, FarParams* out,
+                              CUtensorMap* kmap, CUtensorMap* vmap) {
+  if (!q || !qsl || !seq_lens || !k_cache || !v_cache || !block_table || !o_part || !lse_part)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "window read: null pointer");
+  if (n < 1 || hq < 1 || hkv < 1 || hq % hkv || splits < 1 || splits > 65535 || block_table_len < 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "window read: bad sizes (n, hq, hkv, splits, block table)");
+  if (hd != 128 && hd != 256) return fail(FOLD_ERR_UNSUPPORTED, "window read: head size must be 128 or 256");
+  if (block_size < 16 || block_size % 16)
+    return fail(FOLD_ERR_UNSUPPORTED, "window read: block size must be a positive multiple of 16");
+  if (num_blocks < 1 || num_blocks > (1ll << 31) - 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "window read: number of blocks out of range");
+  if (cache_stride_block <= 0 || cache_stride_head <= 0 || cache_stride_slot <= 0 || cache_stride_block % 8 ||
+      cache_stride_head % 8 || cache_stride_slot % 8 || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(FOLD_ERR_ALIGNMENT, "window read: cache planes must be 16-byte aligned with strides of 8 elements");
+  if (n * (hq / hkv) > 64) return fail(FOLD_ERR_UNSUPPORTED, "window read: n * (hq / hkv) must be at most 64");
+  if (int s = paged_tensor_map(k_cache, num_blocks, block_size, hkv, hd, cache_stride_block, cache_stride_slot,
+                               cache_stride_head, kmap))
+    return s;
+  if (int s = paged_tensor_map(v_cache, num_blocks, block_size, hkv, hd, cache_stride_block, cache_stride_slot,
+                               cache_stride_head, vmap))
+    return s;
+  FarParams prm{};
+  prm.q = static_cast<const __nv_bfloat16*>(q);
+  prm.q_st = q_stride_tok, prm.q_sh = q_stride_head;
+  prm.qsl = qsl, prm.seq = seq_lens;
+  prm.o_part = o_part, prm.lse_part = lse_part;
+  prm.splits = splits, prm.n = n, prm.hq = hq, prm.hkv = hkv, prm.group = hq / hkv;
+  prm.scale_log2 = softmax_scale * kLog2e;
+  prm.err = err;
+  prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, nullptr, 0, 0, nullptr, 0, hd);
+  prm.block_table = block_table, prm.bt_len = block_table_len;
+  prm.num_blocks = static_cast<int>(num_blocks), prm.block_size = block_size;
+  prm.win_left = window_left, prm.win_right = window_right, prm.causal = causal ? 1 : 0;
+  prm.head_inner = cache_stride_head < cache_stride_slot ? 1 : 0;  // as paged_tensor_map orders the dims
+  *out = prm;
+  return FOLD_OK;
+}
+
+// Calls f.run<FarCfg<HD, nt, TK, HG>>() for nt in 1..8 (n * G query rows in n8 tiles).
+template <int HD, int TK, int HG, class F>
+int with_row_tiles(int nt, const F& f) {
+  switch (nt) {
+    case 1: return f.template run<FarCfg<HD, 1, TK, HG>>();
+    case 2: return f.template run<FarCfg<HD, 2, TK, HG>>();
+    case 3: return f.template run<FarCfg<HD, 3, TK, HG>>();
+    case 4: return f.template run<FarCfg<HD, 4, TK, HG>>();
+    case 5: return f.template run<FarCfg<HD, 5, TK, HG>>();
+    case 6: return f.template run<FarCfg<HD, 6, TK, HG>>();
+    case 7: return f.template run<FarCfg<HD, 7, TK, HG>>();
+    case 8: return f.template run<FarCfg<HD, 8, TK, HG>>();
+    default: return fail(FOLD_ERR_UNSUPPORTED, "n * (hq / hkv) must be at most 64");
+  }
+}
+
+// Runs f.run<C>() with the mma.sync configuration of head size hd and n*G rows.
+template <class F>
+int with_mma_config(int hd, int rows, const F& f) {
   const int nt = (rows + 7) / 8;
+  if (hd == 128) return with_row_tiles<128, 128, 4>(nt, f);
+  return with_row_tiles<256, 64, 8>(nt, f);
+}
+
+template <class K>
+static int allow_smem(K kern, int bytes, bool& configured, const char* what) {
+  if (configured) return FOLD_OK;
+  if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what))
+    return s;
+  configured = true;
+  return FOLD_OK;
+}
+
+struct FarLaunch {
+  const FarParams& prm;
+  const void* side;
+  int pages;
+  bool cached_map;  // false: the descriptor is encoded on the stack (no heap use)
+  cudaStream_t stream;
+  template <class C>
+  int run() const {
+    CUtensorMap map;
+    const int s = cached_map ? side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)
+                             : side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map);
+    if (s) return s;
+    static bool configured = false;  // per instantiation
+    if (int e = allow_smem(far_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(far_read)")) return e;
+    far_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
+    return check_launch("far_read_kernel");
+  }
+};
+
+struct WindowLaunch {
+  const FarParams& prm;
+  const CUtensorMap& kmap;
+  const CUtensorMap& vmap;
+  cudaStream_t stream;
+  template <class C>
+  int run() const {
+    static bool configured = false;  // per instantiation
+    if (int e = allow_smem(window_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(window_read)")) return e;
+    window_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(kmap, vmap, prm);
+    return check_launch("window_read_kernel");
+  }
+};
+
+struct StepLaunch {
+  const FarParams& far;
+  const FarParams& win;
+  const void* side;
+  int pages;
+  const CUtensorMap& kmap;
+  const CUtensorMap& vmap;
+  cudaStream_t stream;
+  template <class C>
+  int run() const {
+    CUtensorMap map;
+    if (int s = side_tensor_map(side, pages, far.hkv, C::HD, C::TK, &map)) return s;
+    static bool configured = false;  // per instantiation
+    if (int e = allow_smem(step_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(step_read)")) return e;
+    step_read_kernel<C><<<dim3(win.splits + far.splits, far.hkv), C::NTHREADS, C::SMEM, stream>>>(map, kmap, vmap,
+                                                                                                   far, win);
+    return check_launch("step_read_kernel");
+  }
+};
+
+int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                      const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side,
+                      int pages, int64_t pos_lo, int64_t capacity, int* far_len, float* o_part, float* lse_part,
+                      int splits, int n, int hq, int hkv, int hd, int window, int block, int far_distance,
+                      float softmax_scale, int* err, cudaStream_t stream) {
+  FarParams prm;
+  if (int s = make_far_params(q, q_stride_tok, q_stride_head, qsl, seq_lens, rope_table, table_rows, rot_dim, side,
+                              pages, pos_lo, capacity, far_len, nullptr, 0, 0, o_part, lse_part, splits, n, hq, hkv,
+                              hd, window, block, far_distance, softmax_scale, err, &prm))
+    return s;
+  const int rows = n * (hq / hkv);
   if (far_read_variant(hd, rows) == 1)
     return far_read_tc_launch(prm, side, pages, hd, ((rows + 15) / 16) * 16, false, stream);
-  if (hd == 128) return dispatch_nt_uncached<128, 128, 4>(nt, prm, side, pages, stream);
-  return dispatch_nt_uncached<256, 64, 8>(nt, prm, side, pages, stream);
+  return with_mma_config(hd, rows, FarLaunch{prm, side, pages, false, stream});
 }
 
 }  // namespace fold
@@ -713,38 +937,63 @@ int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, co
                   float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd, int window, int block,
                   int far_distance, float softmax_scale, int* err, void* stream) {
   using namespace fold;
-  if (!q || !qsl || !seq_lens || !side || !o_part || !lse_part)
-    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: null pointer");
-  if (n < 1 || hq < 1 || hkv < 1 || hq % hkv || splits < 1 || pages < 2 || window < 1 || block < 1)
-    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: bad sizes (n, hq, hkv, splits, pages, window, block)");
-  if (splits > 65535) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: too many splits");
-  if (hd != 128 && hd != 256) return fail(FOLD_ERR_UNSUPPORTED, "far read: head size must be 128 or 256");
-  if (rope_table && (rot_dim < 2 || rot_dim % 2 || rot_dim > hd || table_rows < 1))
-    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: bad rotary size or table");
-  if (pos_lo < 0 || pos_lo % 256) return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: pos_lo must be a multiple of 256");
-  if (static_cast<int64_t>(pages) * hkv > (1ll << 31) - 1)
-    return fail(FOLD_ERR_INVALID_ARGUMENT, "far read: side cache too large for one descriptor");
+  FarParams prm;
+  if (int s = make_far_params(q, q_stride_tok, q_stride_head, qsl, seq_lens, rope_table, table_rows, rot_dim, side,
+                              pages, pos_lo, capacity, far_len, qf, qf_stride_tok, qf_stride_head, o_part, lse_part,
+                              splits, n, hq, hkv, hd, window, block, far_distance, softmax_scale, err, &prm))
+    return s;
   const int rows = n * (hq / hkv);
-  if (rows > 64) return fail(FOLD_ERR_UNSUPPORTED, "far read: n * (hq / hkv) must be at most 64");
-  FarParams prm{};
-  prm.q = static_cast<const __nv_bfloat16*>(q);
-  prm.q_st = q_stride_tok, prm.q_sh = q_stride_head;
-  prm.qsl = qsl, prm.seq = seq_lens;
-  prm.table = rope_table, prm.table_rows = table_rows, prm.rot_dim = rot_dim;
-  prm.pos_lo = pos_lo, prm.capacity = capacity, prm.local_cap = static_cast<int64_t>(pages - 1) * 256;
-  prm.far_len = far_len;
-  prm.qf = static_cast<__nv_bfloat16*>(qf), prm.qf_st = qf_stride_tok, prm.qf_sh = qf_stride_head;
-  prm.o_part = o_part, prm.lse_part = lse_part;
-  prm.splits = splits, prm.n = n, prm.hq = hq, prm.hkv = hkv, prm.group = hq / hkv;
-  prm.window = window, prm.block = block, prm.far_distance = far_distance;
-  prm.scale_log2 = softmax_scale * kLog2e;
-  prm.err = err;
-  prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, qf, qf_stride_tok, qf_stride_head, rope_table, rot_dim, hd);
-  const int nt = (rows + 7) / 8;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (far_read_variant(hd, rows) == 1) return far_read_tc_launch(prm, side, pages, hd, ((rows + 15) / 16) * 16, true, s);
-  if (hd == 128) return dispatch_nt<128, 128, 4>(nt, prm, side, pages, s);
-  return dispatch_nt<256, 64, 8>(nt, prm, side, pages, s);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (far_read_variant(hd, rows) == 1) return far_read_tc_launch(prm, side, pages, hd, ((rows + 15) / 16) * 16, true, st);
+  return with_mma_config(hd, rows, FarLaunch{prm, side, pages, true, st});
+}
+
+int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
+                     int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
+                     const int* block_table, int block_table_len, int window_left, int window_right, int causal,
+                     float softmax_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
+                     int* err, void* stream) {
+  using namespace fold;
+  FarParams prm;
+  CUtensorMap kmap, vmap;
+  if (int s = make_window_params(q, q_stride_tok, q_stride_head, qsl, seq_lens, k_cache, v_cache, num_blocks,
+                                 block_size, cache_stride_block, cache_stride_head, cache_stride_slot, block_table,
+                                 block_table_len, window_left, window_right, causal, softmax_scale, o_part, lse_part,
+                                 splits, n, hq, hkv, hd, err, &prm, &kmap, &vmap))
+    return s;
+  return with_mma_config(hd, n * (hq / hkv), WindowLaunch{prm, kmap, vmap, static_cast<cudaStream_t>(stream)});
+}
+
+int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_head, const void* q_win,
+                   int64_t qw_stride_tok, int64_t qw_stride_head, const int* qsl, const int* seq_lens,
+                   const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
+                   int64_t capacity, int* far_len, float* o_fpart, float* lse_fpart, int fsplits,
+                   const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
+                   int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
+                   const int* block_table, int block_table_len, int window_left, int window_right, int causal,
+                   float* o_wpart, float* lse_wpart, int wsplits, int n, int hq, int hkv, int hd, int window,
+                   int block, int far_distance, float far_scale, float win_scale, int* err, void* stream) {
+  using namespace fold;
+  FarParams far, win;
+  CUtensorMap kmap, vmap;
+  if (int s = make_far_params(q_far, qf_stride_tok, qf_stride_head, qsl, seq_lens, rope_table, table_rows, rot_dim,
+                              side, pages, pos_lo, capacity, far_len, nullptr, 0, 0, o_fpart, lse_fpart, fsplits, n,
+                              hq, hkv, hd, window, block, far_distance, far_scale, err, &far))
+    return s;
+  if (int s = make_window_params(q_win, qw_stride_tok, qw_stride_head, qsl, seq_lens, k_cache, v_cache, num_blocks,
+                                 block_size, cache_stride_block, cache_stride_head, cache_stride_slot, block_table,
+                                 block_table_len, window_left, window_right, causal, win_scale, o_wpart, lse_wpart,
+                                 wsplits, n, hq, hkv, hd, err, &win, &kmap, &vmap))
+    return s;
+  if (fsplits + wsplits > 65535) return fail(FOLD_ERR_INVALID_ARGUMENT, "step read: too many splits");
+  const int rows = n * (hq / hkv);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (far_read_variant(hd, rows) == 1) {  // the tcgen05 far read has no window mode: two launches
+    if (int s = far_read_tc_launch(far, side, pages, hd, ((rows + 15) / 16) * 16, true, st)) return s;
+    return with_mma_config(hd, rows, WindowLaunch{win, kmap, vmap, st});
+  }
+  return with_mma_config(hd, rows, StepLaunch{far, win, side, pages, kmap, vmap, st});
 }
 
 }  // extern "C"

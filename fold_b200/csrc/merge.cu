@@ -35,6 +35,28 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
   }
 }
 
+// Both sides as split partials: the window read's splits (pw) are combined by log-sum-exp, then
+// the far read's (pf, which also carries the output and the step geometry), and the two are merged
+// with the alpha weighting. Without far splits the output is the combined window read.
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_partials_kernel(const MergeParams pw, const MergeParams pf, int slices, int hd) {
+  __shared__ SliceSums sums;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = blockIdx.x % slices, th = blockIdx.x / slices;
+  const int t = th / pf.hq, h = th - (th / pf.hq) * pf.hq;
+  const bool active = lane * 4 < min(hd, kSlice);
+  const int col = slice * kSlice + lane * 4;
+  float ol[4], ll;
+  combine_slice(pw, t, h, col, active, true, sums, ol, ll);
+  float of[4] = {0.f, 0.f, 0.f, 0.f}, lf = -INFINITY;
+  if (pf.splits > 0) {
+    __syncthreads();  // warp 0 has read the window sums
+    combine_slice(pf, t, h, col, active, row_has_far(pf, t), sums, of, lf);
+  }
+  if (warp != 0 || !active) return;
+  merge_store_loaded(pf, t, h, col, of, lf, ol, ll);
+}
+
 static int merge_launch(const MergeParams& p, int hd, bool combine, cudaStream_t stream) {
   if (hd < 8 || (hd > kSlice && hd % kSlice) || (hd <= kSlice && hd % 4))
     return fail(FOLD_ERR_UNSUPPORTED, "merge: head size must be a multiple of 128, or of 4 up to 128");
@@ -101,6 +123,38 @@ int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, c
   p.out = static_cast<__nv_bfloat16*>(out), p.out_st = out_stride_tok, p.out_sh = out_stride_head;
   p.qsl = qsl, p.seq = seq_lens, p.n = n, p.hq = hq, p.window = window, p.block = block, p.inv_alpha = inv_alpha;
   return merge_launch(p, hd, false, static_cast<cudaStream_t>(stream));
+}
+
+int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplits, const float* o_fpart,
+                        const float* lse_fpart, int fsplits, void* out, int64_t out_stride_tok,
+                        int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd,
+                        int window, int block, float inv_alpha, void* stream) {
+  using namespace fold;
+  if (!o_wpart || !lse_wpart || !out || !qsl || !seq_lens || (fsplits > 0 && (!o_fpart || !lse_fpart)))
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: null pointer");
+  if (n < 1 || hq < 1 || wsplits < 1 || fsplits < 0) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: bad sizes");
+  if (hd < 8 || (hd > kSlice && hd % kSlice) || (hd <= kSlice && hd % 4))
+    return fail(FOLD_ERR_UNSUPPORTED, "merge partials: head size must be a multiple of 128, or of 4 up to 128");
+  if (out_stride_tok % 2 || out_stride_head % 2 || (reinterpret_cast<uintptr_t>(out) & 3) ||
+      (reinterpret_cast<uintptr_t>(o_wpart) & 7) || (reinterpret_cast<uintptr_t>(o_fpart) & 7))
+    return fail(FOLD_ERR_ALIGNMENT, "merge partials: rows must start on element pairs");
+  MergeParams pw{}, pf{};
+  for (MergeParams* p : {&pw, &pf}) {
+    p->of_bf16 = 0;
+    p->of_ss = static_cast<int64_t>(n) * hq * hd, p->of_st = static_cast<int64_t>(hq) * hd, p->of_sh = hd;
+    p->lf_ss = static_cast<int64_t>(hq) * n, p->lf_sh = n, p->lf_st = 1;
+    p->qsl = qsl, p->seq = seq_lens, p->n = n, p->hq = hq;
+  }
+  pw.o_f = o_wpart, pw.lse_f = lse_wpart, pw.splits = wsplits;
+  pf.o_f = o_fpart, pf.lse_f = lse_fpart, pf.splits = fsplits;
+  pf.out = static_cast<__nv_bfloat16*>(out), pf.out_st = out_stride_tok, pf.out_sh = out_stride_head;
+  pf.window = window, pf.block = block, pf.inv_alpha = inv_alpha;
+  const int slices = hd > kSlice ? hd / kSlice : 1;
+  const int64_t blocks = static_cast<int64_t>(n) * hq * slices;
+  if (blocks > 2147483647) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: too many rows");
+  merge_partials_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      pw, pf, slices, hd);
+  return check_launch("merge_partials_kernel");
 }
 
 int fold_combine(const float* o_part, const float* lse_part, int splits, float* o_out, float* lse_out, int n, int hq,

@@ -115,6 +115,51 @@ def merge(out_l, lse_l, out_f, lse_f, out, qsl, seq_lens, *, window, block, alph
               1.0 / float(alpha), _stream(out))
 
 
+def _check_partials(o_part, lse_part, n, hq, d, what):
+    splits = o_part.shape[0]
+    if o_part.shape != (splits, n, hq, d) or lse_part.shape != (splits, hq, n) or not o_part.is_contiguous() \
+            or not lse_part.is_contiguous() or o_part.dtype != torch.float32 or lse_part.dtype != torch.float32:
+        raise FoldError(f"{what}: partials must be contiguous float32 [S, n, Hq, D] and [S, Hq, n]")
+    return splits
+
+
+def _side_args(q, side, table, rot_dim, pos_lo, capacity, far_len):
+    """(q, C-ABI arguments from the rope table to far_len) of a far read of `side`."""
+    n, hq, d = q.shape
+    pages = side.shape[0]
+    if side.dtype != torch.bfloat16 or q.dtype != torch.bfloat16:
+        raise FoldError("far_read: q and the side cache must be bfloat16")
+    if not side.is_contiguous() or side.shape[2] != SIDE_BLOCK or side.shape[3] != 2 * d:
+        raise FoldError("far_read: side cache must be a contiguous [pages, Hkv, 256, 2 * head_dim] tensor")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if capacity is None:
+        capacity = int(pos_lo) + (pages - 1) * SIDE_BLOCK
+    if table is not None and rot_dim is None:
+        rot_dim = table.shape[1]
+    return q, (_p(table), 0 if table is None else table.shape[0], 0 if table is None else int(rot_dim), _p(side),
+               pages, int(pos_lo), int(capacity), _p(far_len))
+
+
+def _paged_args(q, k_cache, v_cache, block_table, window_size, causal):
+    """(q, C-ABI arguments from the cache planes to `causal`) of a window read."""
+    n, hq, d = q.shape
+    nb, hkv, bs, dk = k_cache.shape
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise FoldError("window_read: q and the cache must be bfloat16")
+    if v_cache.shape != k_cache.shape or dk != d or k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1:
+        raise FoldError("window_read: K and V planes must be [num_blocks, Hkv, block_size, head_dim] views with "
+                        "equal strides and a contiguous head dimension")
+    if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
+        raise FoldError("window_read: block_table must be int32 with contiguous rows")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    left, right = (int(w) for w in window_size)
+    st_block, st_head, st_slot = k_cache.stride()[:3]
+    return q, (_p(k_cache), _p(v_cache), nb, bs, st_block, st_head, st_slot, _p(block_table), block_table.shape[-1],
+               left, right, int(bool(causal)))
+
+
 def far_read(q, qsl, seq_lens, side, o_part, lse_part, *, window, block, far_distance, softmax_scale,
              table=None, rot_dim=None, far_len=None, qf=None, pos_lo=0, capacity=None, err=None):
     """Split-KV read of the side cache with the far-query rotation fused in.
@@ -126,26 +171,82 @@ def far_read(q, qsl, seq_lens, side, o_part, lse_part, *, window, block, far_dis
     _require_cuda(q, qsl, seq_lens, side, o_part, lse_part, table, far_len, qf, err)
     _check_lengths(qsl, seq_lens)
     n, hq, d = q.shape
-    pages, hkv = side.shape[0], side.shape[1]
-    if side.dtype != torch.bfloat16 or q.dtype != torch.bfloat16:
-        raise FoldError("far_read: q and the side cache must be bfloat16")
-    if not side.is_contiguous() or side.shape[2] != SIDE_BLOCK or side.shape[3] != 2 * d:
-        raise FoldError("far_read: side cache must be a contiguous [pages, Hkv, 256, 2 * head_dim] tensor")
-    splits = o_part.shape[0]
-    if o_part.shape != (splits, n, hq, d) or lse_part.shape != (splits, hq, n) or not o_part.is_contiguous() \
-            or not lse_part.is_contiguous() or o_part.dtype != torch.float32 or lse_part.dtype != torch.float32:
-        raise FoldError("far_read: partials must be contiguous float32 [S, n, Hq, D] and [S, Hq, n]")
-    if q.stride(-1) != 1:
-        q = q.contiguous()
-    if capacity is None:
-        capacity = int(pos_lo) + (pages - 1) * SIDE_BLOCK
-    if table is not None and rot_dim is None:
-        rot_dim = table.shape[1]
-    _lib.call("fold_far_read", _p(q), q.stride(0), q.stride(1), _p(qsl), _p(seq_lens), _p(table),
-              0 if table is None else table.shape[0], 0 if table is None else int(rot_dim), _p(side), pages,
-              int(pos_lo), int(capacity), _p(far_len), _p(qf), 0 if qf is None else qf.stride(0),
-              0 if qf is None else qf.stride(1), _p(o_part), _p(lse_part), splits, n, hq, hkv, d, int(window),
-              int(block), int(far_distance), float(softmax_scale), _p(err), _stream(q))
+    splits = _check_partials(o_part, lse_part, n, hq, d, "far_read")
+    q, side_args = _side_args(q, side, table, rot_dim, pos_lo, capacity, far_len)
+    _lib.call("fold_far_read", _p(q), q.stride(0), q.stride(1), _p(qsl), _p(seq_lens), *side_args, _p(qf),
+              0 if qf is None else qf.stride(0), 0 if qf is None else qf.stride(1), _p(o_part), _p(lse_part), splits,
+              n, hq, side.shape[1], d, int(window), int(block), int(far_distance), float(softmax_scale), _p(err),
+              _stream(q))
+
+
+def paged_planes(kv_cache, head_dim):
+    """K and V planes [num_blocks, Hkv, block_size, D] of vLLM's FlashAttention cache
+    kv_cache[num_blocks, Hkv, block_size, 2 * D] (views, no copy)."""
+    return kv_cache[..., :head_dim], kv_cache[..., head_dim:]
+
+
+def window_read(q, qsl, seq_lens, k_cache, v_cache, block_table, o_part, lse_part, *, window_size, causal,
+                softmax_scale, err=None):
+    """Exact-position window read of a paged cache into split partials (the FlashAttention window
+    read of fold/attention.py:148-151,163 and :211-215).
+
+    q [n, Hq, D] bf16 (RoPE'd); k_cache, v_cache [num_blocks, Hkv, block_size, D] bf16 planes with
+    equal strides (paged_planes of vLLM's cache); block_table int32 [1, max_blocks] or
+    [max_blocks]; window_size (left, right) as FlashAttention's (-1: unbounded). o_part
+    [S, n, Hq, D] and lse_part [S, Hq, n] float32 receive one partial per split."""
+    _require_cuda(q, qsl, seq_lens, k_cache, v_cache, block_table, o_part, lse_part, err)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = q.shape
+    splits = _check_partials(o_part, lse_part, n, hq, d, "window_read")
+    q, paged = _paged_args(q, k_cache, v_cache, block_table, window_size, causal)
+    _lib.call("fold_window_read", _p(q), q.stride(0), q.stride(1), _p(qsl), _p(seq_lens), *paged, float(softmax_scale),
+              _p(o_part), _p(lse_part), splits, n, hq, k_cache.shape[1], d, _p(err), _stream(q))
+
+
+def step_read(q_far, q_win, qsl, seq_lens, side, far_parts, k_cache, v_cache, block_table, window_parts, *, window,
+              block, far_distance, softmax_scale, alpha, window_size, causal, table=None, rot_dim=None,
+              far_len=None, pos_lo=0, capacity=None, err=None):
+    """The far read (as far_read, of q_far) and the window read (as window_read, of q_win) of one
+    draft step in one launch: per KV head the window read's splits run beside the far read's.
+    far_parts and window_parts are (o, lse) split buffers; the far softmax scale is
+    alpha * softmax_scale, the window's softmax_scale."""
+    (fo_, fl_), (wo_, wl_) = far_parts, window_parts
+    _require_cuda(q_far, q_win, qsl, seq_lens, side, fo_, fl_, k_cache, v_cache, block_table, wo_, wl_, table,
+                  far_len, err)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = q_far.shape
+    if q_win.shape != q_far.shape:
+        raise FoldError("step_read: the far and window queries must have the same shape")
+    fsplits = _check_partials(fo_, fl_, n, hq, d, "step_read")
+    wsplits = _check_partials(wo_, wl_, n, hq, d, "step_read")
+    q_far, side_args = _side_args(q_far, side, table, rot_dim, pos_lo, capacity, far_len)
+    q_win, paged = _paged_args(q_win, k_cache, v_cache, block_table, window_size, causal)
+    _lib.call("fold_step_read", _p(q_far), q_far.stride(0), q_far.stride(1), _p(q_win), q_win.stride(0),
+              q_win.stride(1), _p(qsl), _p(seq_lens), *side_args, _p(fo_), _p(fl_), fsplits, *paged, _p(wo_), _p(wl_),
+              wsplits, n, hq, side.shape[1], d, int(window), int(block), int(far_distance),
+              float(softmax_scale) * float(alpha), float(softmax_scale), _p(err), _stream(q_far))
+
+
+def merge_partials(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens, *, window, block, alpha):
+    """Writes into out [n, Hq, D] bf16 the alpha-weighted merge (fold/kernels.py:135-142) of the
+    window read's split partials (o_wpart [Sw, n, Hq, D], lse_wpart [Sw, Hq, n]) with the far
+    read's (o_fpart [Sf, n, Hq, D], lse_fpart [Sf, Hq, n]); with o_fpart None the combined window
+    read alone."""
+    _require_cuda(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens)
+    _check_lengths(qsl, seq_lens)
+    sw, n, hq, d = o_wpart.shape
+    sf = 0 if o_fpart is None else o_fpart.shape[0]
+    for o, l, s in ((o_wpart, lse_wpart, sw), (o_fpart, lse_fpart, sf)):
+        if o is None:
+            continue
+        if o.shape != (s, n, hq, d) or l.shape != (s, hq, n) or o.dtype != torch.float32 \
+                or l.dtype != torch.float32 or not o.is_contiguous() or not l.is_contiguous():
+            raise FoldError("merge_partials: partials must be contiguous float32 [S, n, Hq, D] and [S, Hq, n]")
+    if out.dtype != torch.bfloat16 or out.stride(-1) != 1 or out.shape != (n, hq, d):
+        raise FoldError("merge_partials: out must be bfloat16 [n, Hq, D] with a contiguous head dimension")
+    _lib.call("fold_merge_partials", _p(o_wpart), _p(lse_wpart), sw, _p(o_fpart), _p(lse_fpart), sf, _p(out),
+              out.stride(0), out.stride(1), _p(qsl), _p(seq_lens), n, hq, d, int(window), int(block),
+              1.0 / float(alpha), _stream(out))
 
 
 def append(k, v, positions, slots, side, *, pos_lo=0, skip_foreign=False, err=None):

@@ -43,6 +43,7 @@ enum fold_status {
 #define FOLD_DEVERR_ROPE_RANGE 2   /* |rotation offset| beyond the rope table (offset clamped) */
 #define FOLD_DEVERR_TIMEOUT 4      /* a pipeline wait of the far read, or a wait for a peer, gave up */
 #define FOLD_DEVERR_CAPACITY 8     /* far_len exceeds the side cache's capacity */
+#define FOLD_DEVERR_BLOCK_TABLE 16 /* a window-read block-table entry lies outside the paged cache */
 
 const char* fold_status_string(int status);
 const char* fold_last_error(void);
@@ -104,6 +105,50 @@ int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, co
                   float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd, int window, int block,
                   int far_distance, float softmax_scale, int* err, void* stream);
 
+/* Window (exact-position) read of the paged drafter cache. Replaces the FlashAttention window
+ * read of fold/attention.py:148-151,163 (window_size = [W + B - 1, B - 1], causal = False) and of
+ * the sliding layers, :211-215 (the native window, causal), with split partials instead of one
+ * output. q: RoPE'd queries [n, hq, hd] bf16; row r sits at position p = H + r
+ * (FlashAttention's bottom-right alignment, H = seq_lens[0] - qlen) and reads the cached
+ * positions j with p - window_left <= j <= p + window_right (a negative bound is unbounded),
+ * j <= p when `causal`, and j < seq_lens[0]. k_cache and v_cache are the K and V planes of the
+ * paged cache, [num_blocks, hkv, block_size, hd] bf16 with the given strides (elements, multiples
+ * of 8; innermost dim contiguous; both planes share them): for vLLM's FlashAttention cache
+ * kv[num_blocks, hkv, block_size, 2*hd], k_cache = kv, v_cache = kv + hd. block_table[i] is the
+ * cache block of positions [i*block_size, (i+1)*block_size) (block_table_len entries; an entry
+ * outside [0, num_blocks) sets FOLD_DEVERR_BLOCK_TABLE). block_size is a multiple of 16. Each of
+ * `splits` CTAs per KV head reads a contiguous range of the window and writes a normalised
+ * partial: o_part [splits, n, hq, hd], lse_part [splits, hq, n] float32 (natural log of the sum of
+ * exp(softmax_scale * q.k); -inf for a split without keys). hd in {128, 256},
+ * n * (hq / hkv) <= 64. */
+int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
+                     int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
+                     const int* block_table, int block_table_len, int window_left, int window_right, int causal,
+                     float softmax_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
+                     int* err, void* stream);
+
+/* The far read and the window read of one draft step in one launch. Replaces, for a full-attention
+ * FOLD layer, far_query + both FlashAttention reads of fold/attention.py:162-170. Arguments as
+ * fold_far_read (q_far, the rope table, the side cache, far_len, the far partials o_fpart/lse_fpart
+ * with fsplits splits, far_scale = alpha * scale) and as fold_window_read (q_win, the paged cache,
+ * its block table, the window, the window partials o_wpart/lse_wpart with wsplits splits,
+ * win_scale = scale). Per KV head, wsplits CTAs read the window while fsplits CTAs read the far
+ * memory, so the window read (a few MB) runs beside the far read instead of after it; choose
+ * wsplits + fsplits <= SMs / hkv to keep one wave (e.g. wsplits = 1,
+ * fsplits = fold_far_read_default_splits - 1). When the far read takes the tcgen05 kernel (see
+ * fold_far_read_select_kernel) the two reads are issued as two launches. Merge the result with
+ * fold_merge_partials. */
+int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_head, const void* q_win,
+                   int64_t qw_stride_tok, int64_t qw_stride_head, const int* qsl, const int* seq_lens,
+                   const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
+                   int64_t capacity, int* far_len, float* o_fpart, float* lse_fpart, int fsplits,
+                   const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
+                   int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
+                   const int* block_table, int block_table_len, int window_left, int window_right, int causal,
+                   float* o_wpart, float* lse_wpart, int wsplits, int n, int hq, int hkv, int hd, int window,
+                   int block, int far_distance, float far_scale, float win_scale, int* err, void* stream);
+
 /* Chooses the far-read kernel for later calls: 0 = mma.sync tiles, 1 = tcgen05 tiles with TMEM
  * accumulators, -1 = per shape (the default: tcgen05 above 48 query rows per KV head). Both give
  * the same results within rounding. The environment variable FOLD_FAR_READ_KERNEL=mma|tc sets
@@ -126,6 +171,18 @@ int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, c
                int64_t lf_stride_head, int64_t lf_stride_tok, int splits, void* out, int64_t out_stride_tok,
                int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd, int window,
                int block, float inv_alpha, void* stream);
+
+/* LSE merge of two sets of split partials. Replaces merge / _merge_kernel
+ * (fold/kernels.py:86-108,135-142) together with both FlashAttention split combines: the window
+ * read's wsplits partials (o_wpart [wsplits, n, hq, hd], lse_wpart [wsplits, hq, n], as written
+ * by fold_window_read) and the far read's fsplits partials (as written by fold_far_read) are each
+ * combined by log-sum-exp, then merged with the alpha weighting of fold_merge. fsplits = 0 (far
+ * pointers may then be NULL) writes the combined window read alone (the window ablation and plain
+ * sliding layers). All partials float32 and contiguous; out bf16 with strides (tok, head). */
+int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplits, const float* o_fpart,
+                        const float* lse_fpart, int fsplits, void* out, int64_t out_stride_tok,
+                        int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd,
+                        int window, int block, float inv_alpha, void* stream);
 
 /* Log-sum-exp combine of `splits` partials o_part [splits, n, hq, hd], lse_part [splits, hq, n]
  * (float32, contiguous) into one partial o_out [n, hq, hd], lse_out [hq, n]. Used on each rank

@@ -59,6 +59,25 @@ def side_from(k, v, pages, device="cuda"):
     return bf16_tensor(side.reshape(pages, hkv, fo.SIDE_BLOCK, 2 * d), device)
 
 
+def paged_from(k, v, block_size, rng, spare_blocks=3, fill=np.nan, device="cuda"):
+    """vLLM's FlashAttention cache kv[num_blocks, Hkv, block_size, 2D] (bf16) holding K, V
+    [L, Hkv, D] at positions 0..L-1 in shuffled blocks; every other slot holds `fill` (NaN by
+    default: the window read must neither use nor be poisoned by it). Returns kv and the block
+    table int32 [1, blocks + 2] (the trailing entries are 0, as vLLM pads)."""
+    L, hkv, d = k.shape
+    nbl = -(-L // block_size)
+    nb = nbl + spare_blocks
+    perm = rng.permutation(nb)[:nbl]
+    kv = np.full((nb, hkv, block_size, 2 * d), fill, dtype=np.float32)
+    pos = np.arange(L)
+    blk, off = perm[pos // block_size], pos % block_size
+    kv[blk, :, off, :d] = k
+    kv[blk, :, off, d:] = v
+    table = np.zeros((1, nbl + 2), dtype=np.int32)
+    table[0, :nbl] = perm
+    return bf16_tensor(kv, device), torch.from_numpy(table).to(device)
+
+
 def torch_local_read(q, kv_cache, meta, original, *, window_size, causal, num_splits):
     """float32 torch window read over a contiguous [seq, 2, Hkv, D] cache (test stand-in for the
     FlashAttention read; FlashAttention semantics: bottom-right aligned window)."""

@@ -1,8 +1,10 @@
 """The FOLD forward (FoldAttention.forward with the reference's signature) and the side-cache
 append path, on the GPU, against the reference's own fold_block outputs (tests/golden).
 
-The window read is a float32 torch stand-in for FlashAttention (it is outside the kernels of this
-package); the far read, the rotation, the merge and the append are the CUDA library."""
+Every kernel of the step is the CUDA library: the window read over a paged cache in vLLM's
+FlashAttention layout (shuffled blocks, NaN in every unused slot), the rotated far read, the merge
+of both split sets and the append. One test replaces the window read through the `local_read`
+hook with a float32 torch read."""
 from types import SimpleNamespace
 
 import numpy as np
@@ -11,7 +13,7 @@ import torch
 
 from fold_b200.attention import FoldAttention, FoldWorkspace, SlidingFoldAttention
 from oracle import fold_oracle as fo
-from tests.helpers import OUT_ATOL, bf16_tensor, golden_block_case, golden_block_names, torch_local_read
+from tests.helpers import OUT_ATOL, bf16_tensor, golden_block_case, golden_block_names, paged_from, torch_local_read
 
 pytestmark = pytest.mark.gpu
 
@@ -19,9 +21,10 @@ if not torch.cuda.is_available():
     pytest.skip("needs a CUDA GPU", allow_module_level=True)
 
 
-def build_step(g, device="cuda", sliding=False):
-    """Buffers of one draft step for a golden case: RoPE'd query and local cache, side cache
-    filled through the append kernel (keys before RoPE), fake vLLM layer and metadata."""
+def build_step(g, device="cuda", sliding=False, paged=True, block_size=16):
+    """Buffers of one draft step for a golden case: RoPE'd query and drafter cache (paged, or
+    [seq, 2, hkv, d] for the torch read), side cache filled through the append kernel (keys before
+    RoPE), fake vLLM layer and metadata."""
     q, kc, vc, kb, vb = g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"]
     t, B = kc.shape[0], q.shape[0]
     hq, hkv, d = q.shape[1], kc.shape[1], q.shape[2]
@@ -30,7 +33,11 @@ def build_step(g, device="cuda", sliding=False):
     vals = np.concatenate((vc, vb))
     k_roped = fo.rotate(keys, np.arange(t + B), f)
     q_roped = fo.rotate(q, np.arange(t, t + B), f)
-    kv_cache = torch.stack((bf16_tensor(k_roped, device), bf16_tensor(vals, device)), dim=1)  # [seq, 2, hkv, d]
+    table = None
+    if paged:
+        kv_cache, table = paged_from(k_roped, vals, block_size, np.random.default_rng(t), device=device)
+    else:
+        kv_cache = torch.stack((bf16_tensor(k_roped, device), bf16_tensor(vals, device)), dim=1)  # [seq, 2, hkv, d]
     dummy_cache = torch.zeros((1, hkv, 16, 2 * d), device=device, dtype=torch.bfloat16)
     W = g["window"]
     inv = torch.from_numpy(f).to(device)
@@ -43,7 +50,7 @@ def build_step(g, device="cuda", sliding=False):
                                vllm_flash_attn_version=4)
     meta = SimpleNamespace(num_actual_tokens=B, query_start_loc=torch.tensor([0, B], dtype=torch.int32, device=device),
                            seq_lens=torch.tensor([t + B], dtype=torch.int32, device=device), max_query_len=B,
-                           max_seq_len=t + B, block_table=None, use_cascade=False, causal=True)
+                           max_seq_len=t + B, block_table=table, use_cascade=False, causal=True)
     query = bf16_tensor(q_roped, device)
     output = torch.empty((B, hq * d), device=device, dtype=torch.bfloat16)
     return ws, original, meta, query, kv_cache, output
@@ -56,7 +63,7 @@ CASES = golden_block_names(min_hd=128)
 def test_fold_forward_matches_reference(name, far_kernel):
     g = golden_block_case(name)
     ws, original, meta, query, kv_cache, output = build_step(g)
-    layer = FoldAttention(original, ws, local_read=torch_local_read)
+    layer = FoldAttention(original, ws)
     out = layer.forward(None, query, None, None, kv_cache, meta, output)
     torch.cuda.synchronize()
     ws.check()
@@ -64,12 +71,31 @@ def test_fold_forward_matches_reference(name, far_kernel):
     assert np.abs(got - g["out"]).max() <= OUT_ATOL
 
 
+@pytest.mark.parametrize("block_size", [32, 256])
+def test_fold_forward_block_sizes(block_size):
+    g = golden_block_case(CASES[-1])
+    ws, original, meta, query, kv_cache, output = build_step(g, block_size=block_size)
+    out = FoldAttention(original, ws).forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    ws.check()
+    assert np.abs(out.float().cpu().numpy().reshape(g["out"].shape) - g["out"]).max() <= OUT_ATOL
+
+
+def test_local_read_hook_replaces_the_window_read():
+    g = golden_block_case(CASES[0])
+    ws, original, meta, query, kv_cache, output = build_step(g, paged=False)
+    out = FoldAttention(original, ws, local_read=torch_local_read).forward(None, query, None, None, kv_cache, meta,
+                                                                            output)
+    torch.cuda.synchronize()
+    assert np.abs(out.float().cpu().numpy().reshape(g["out"].shape) - g["out"]).max() <= OUT_ATOL
+
+
 @pytest.mark.parametrize("name", CASES[:3])
 def test_sliding_fold_forward_matches_reference(name):
     """sliding_layers="fold": native causal window (W + B - 1, 0) as the local branch."""
     g = golden_block_case(name)
     ws, original, meta, query, kv_cache, output = build_step(g, sliding=True)
-    layer = SlidingFoldAttention(original, ws, local_read=torch_local_read)
+    layer = SlidingFoldAttention(original, ws)
     out = layer.forward(None, query, None, None, kv_cache, meta, output)
     torch.cuda.synchronize()
     # with the native window W + B - 1 the native read sees the same near set as FOLD, except the
@@ -95,10 +121,36 @@ def test_window_mode_and_empty_step():
     g = golden_block_case(CASES[0])
     ws, original, meta, query, kv_cache, output = build_step(g)
     ws.mode = "window"
-    layer = FoldAttention(original, ws, local_read=torch_local_read)
+    layer = FoldAttention(original, ws)
     out = layer.forward(None, query, None, None, kv_cache, meta, output)
-    o_l, _ = torch_local_read(query, kv_cache, meta, original, window_size=(ws.window + ws.block - 1,
-                                                                             ws.block - 1), causal=False, num_splits=1)
-    assert torch.equal(out, o_l.reshape(out.shape))
+    torch.cuda.synchronize()
+    q, kc, vc, kb, vb = g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"]
+    t, B = kc.shape[0], q.shape[0]
+    f = g["inv_freq"]
+    k_roped = fo.bf16_round(fo.rotate(np.concatenate((kc, kb)), np.arange(t + B), f))
+    q_roped = fo.bf16_round(fo.rotate(q, np.arange(t, t + B), f))
+    o_l, _ = fo.local_read(q_roped, k_roped, fo.bf16_round(np.concatenate((vc, vb))), t, ws.window, B, g["scale"])
+    assert np.abs(out.float().cpu().numpy().reshape(o_l.shape) - o_l).max() <= OUT_ATOL
     meta.num_actual_tokens = 0
     assert torch.count_nonzero(layer.forward(None, query, None, None, kv_cache, meta, output)) == 0
+
+
+def test_native_window_layer_matches_oracle():
+    """sliding_layers="window": the plain native causal read, no memory (fold/attention.py:98-123)."""
+    from fold_b200.attention import NativeWindowAttention
+    g = golden_block_case(CASES[0])
+    ws, original, meta, query, kv_cache, output = build_step(g)
+    native = 300
+    original.sliding_window = (native, 0)
+    layer = NativeWindowAttention(original, block=query.shape[0], device=query.device)
+    out = layer.forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    layer.check()
+    q, kc, vc, kb, vb = g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"]
+    t, B = kc.shape[0], q.shape[0]
+    f = g["inv_freq"]
+    k_roped = fo.bf16_round(fo.rotate(np.concatenate((kc, kb)), np.arange(t + B), f))
+    q_roped = fo.bf16_round(fo.rotate(q, np.arange(t, t + B), f))
+    want, _ = fo.window_read(q_roped, k_roped, fo.bf16_round(np.concatenate((vc, vb))), t, native, 0, True,
+                             g["scale"])
+    assert np.abs(out.float().cpu().numpy().reshape(want.shape) - want).max() <= OUT_ATOL
