@@ -119,41 +119,61 @@ __device__ __forceinline__ void issue_window_tile(unsigned char* smem, uint64_t*
   }
 }
 
-// Vectorised far-query rotation: each work item is one row's pair of 8-element chunks
-// ([8c, 8c+8) with its neox partner [RH+8c, ...), or 16 unrotated elements), loaded as 16-byte
-// vectors. Every thread issues the loads of all its items before any arithmetic, so the prologue
-// costs one memory latency instead of one per element.
+// One thread's share of a CTA's query rows for the vectorised rotation: each work item is one
+// row's pair of 8-element chunks ([8c, 8c+8) with its neox partner [RH+8c, ...), or 16 unrotated
+// elements), held as 16-byte vectors. The loads are issued first thing in the kernel (they depend
+// on nothing the kernel reads), so their latency overlaps the step-length and table reads.
 template <class C>
-__device__ __forceinline__ void rotate_query_vec(const FarParams& p, const float* trow, int RH, float sgn, int h,
-                                                 int split, int nrows, int G, __nv_bfloat16* Qs) {
-  constexpr int PAIRS = C::HD / 16;
-  constexpr int ITEMS = C::ROWS * PAIRS;
-  constexpr int MAXI = (ITEMS + C::NTHREADS - 1) / C::NTHREADS;
-  const int tid = threadIdx.x;
-  const int rh8 = trow ? RH / 8 : 0;
-  uint4 qa[MAXI], qb[MAXI];
-  float4 c0[MAXI], c1[MAXI], s0[MAXI], s1[MAXI];
+struct QueryLoad {
+  static constexpr int PAIRS = C::HD / 16;
+  static constexpr int ITEMS = C::ROWS * PAIRS;
+  static constexpr int MAXI = (ITEMS + C::NTHREADS - 1) / C::NTHREADS;
+  uint4 a[MAXI], b[MAXI];
+};
+
+// rh8 = rotated 8-element chunks per half (0: no rotation).
+template <class C>
+__device__ __forceinline__ void load_query_vec(const FarParams& p, int rh8, int RH, int h, int nrows, int G,
+                                               QueryLoad<C>& ql) {
+  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS;
 #pragma unroll
-  for (int k = 0; k < MAXI; ++k) {
-    const int e = tid + k * C::NTHREADS;
-    qa[k] = qb[k] = make_uint4(0, 0, 0, 0);
-    c0[k] = c1[k] = s0[k] = s1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < QueryLoad<C>::MAXI; ++k) {
+    const int e = threadIdx.x + k * C::NTHREADS;
+    ql.a[k] = ql.b[k] = make_uint4(0, 0, 0, 0);
     if (e < ITEMS) {
       const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
       if (rho < nrows) {
         const int r = rho / G, hq = h * G + (rho - r * G);
         const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
-        if (c < rh8) {
-          qa[k] = __ldg(reinterpret_cast<const uint4*>(qr + 8 * c));
-          qb[k] = __ldg(reinterpret_cast<const uint4*>(qr + RH + 8 * c));
-          const float4* tc = reinterpret_cast<const float4*>(trow + 8 * c);
-          const float4* ts = reinterpret_cast<const float4*>(trow + RH + 8 * c);
-          c0[k] = __ldg(tc), c1[k] = __ldg(tc + 1), s0[k] = __ldg(ts), s1[k] = __ldg(ts + 1);
-        } else {
-          const int off = 2 * RH * (rh8 > 0) + 16 * (c - rh8);
-          qa[k] = __ldg(reinterpret_cast<const uint4*>(qr + off));
-          qb[k] = __ldg(reinterpret_cast<const uint4*>(qr + off + 8));
-        }
+        const int off_a = c < rh8 ? 8 * c : 2 * RH * (rh8 > 0) + 16 * (c - rh8);
+        const int off_b = c < rh8 ? RH + 8 * c : off_a + 8;
+        ql.a[k] = __ldg(reinterpret_cast<const uint4*>(qr + off_a));
+        ql.b[k] = __ldg(reinterpret_cast<const uint4*>(qr + off_b));
+      }
+    }
+  }
+}
+
+// Vectorised far-query rotation of the loaded rows with the table row `trow` (cos then sin; read
+// only when rh8 > 0), written to the query tile Qs (and to qf by split 0). Every thread issues its
+// table loads before any arithmetic, so this costs one memory latency.
+template <class C>
+__device__ __forceinline__ void rotate_query_vec(const FarParams& p, const QueryLoad<C>& ql, const float* trow,
+                                                 int rh8, int RH, float sgn, int h, int split, int nrows, int G,
+                                                 __nv_bfloat16* Qs) {
+  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS, MAXI = QueryLoad<C>::MAXI;
+  const int tid = threadIdx.x;
+  float4 c0[MAXI], c1[MAXI], s0[MAXI], s1[MAXI];
+#pragma unroll
+  for (int k = 0; k < MAXI; ++k) {
+    const int e = tid + k * C::NTHREADS;
+    c0[k] = c1[k] = s0[k] = s1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < ITEMS) {
+      const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
+      if (rho < nrows && c < rh8) {
+        const float4* tc = reinterpret_cast<const float4*>(trow + 8 * c);
+        const float4* ts = reinterpret_cast<const float4*>(trow + RH + 8 * c);
+        c0[k] = __ldg(tc), c1[k] = __ldg(tc + 1), s0[k] = __ldg(ts), s1[k] = __ldg(ts + 1);
       }
     }
   }
@@ -163,13 +183,13 @@ __device__ __forceinline__ void rotate_query_vec(const FarParams& p, const float
     if (e >= ITEMS) continue;
     const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
     int off_a, off_b;
-    uint4 ya = qa[k], yb = qb[k];
+    uint4 ya = ql.a[k], yb = ql.b[k];
     if (c < rh8) {
       off_a = 8 * c, off_b = RH + 8 * c;
       const float cs[8] = {c0[k].x, c0[k].y, c0[k].z, c0[k].w, c1[k].x, c1[k].y, c1[k].z, c1[k].w};
       const float sn[8] = {s0[k].x, s0[k].y, s0[k].z, s0[k].w, s1[k].x, s1[k].y, s1[k].z, s1[k].w};
-      const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&qa[k]);
-      const __nv_bfloat162* xb = reinterpret_cast<const __nv_bfloat162*>(&qb[k]);
+      const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&ql.a[k]);
+      const __nv_bfloat162* xb = reinterpret_cast<const __nv_bfloat162*>(&ql.b[k]);
       uint32_t* oa = reinterpret_cast<uint32_t*>(&ya);
       uint32_t* ob = reinterpret_cast<uint32_t*>(&yb);
 #pragma unroll
@@ -242,6 +262,12 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.y;
+  const int G = p.group;
+  const int nrows = p.n * G;
+  const int RH = p.rot_dim >> 1;
+  const int rh8 = (!WIN && p.table) ? RH / 8 : 0;  // the far read rotates when it has a table
+  QueryLoad<C> ql;
+  if (p.vec_rot) load_query_vec<C>(p, rh8, RH, h, nrows, G, ql);
 
   // Step geometry, from the device-side lengths (fold/kernels.py:24-30).
   const int qlen = p.qsl[1] - p.qsl[0];
@@ -292,15 +318,11 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
   }
 
-  const int G = p.group;
-  const int nrows = p.n * G;
-
   // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table.
   // The window read takes the query as it is.
   {
     const float* trow = nullptr;
     float sgn = 1.f;
-    const int RH = p.rot_dim >> 1;
     if constexpr (!WIN) {
       const int delta = p.far_distance - hist;
       int ad = delta < 0 ? -delta : delta;
@@ -312,7 +334,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
     }
     if (p.vec_rot) {
-      rotate_query_vec<C>(p, trow, RH, sgn, h, split, nrows, G, Qs);
+      rotate_query_vec<C>(p, ql, trow, rh8, RH, sgn, h, split, nrows, G, Qs);
     } else {
       for (int e = tid; e < ROWS * HD; e += NTH) {
         const int rho = e / HD, d = e - (e / HD) * HD;
