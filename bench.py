@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1: how the per-rank partials meet (peer-to-peer kernel, or NCCL all-gather + merge)")
+    ap.add_argument("--fused", action="store_true",
+                    help="run the far read and the merge (or the peer exchange) as one cooperative kernel instead "
+                         "of two launches")
     return ap.parse_args()
 
 
@@ -281,7 +284,10 @@ def run_gpu(args):
     o_mine, lse_mine = send[: B * hq * hd].view(B, hq, hd), send[B * hq * hd:].view(hq, B)
     scale = hd ** -0.5 * ALPHA
     stream = torch.cuda.current_stream(dev)
-    peer = PeerExchange(n=B, hq=hq, hd=hd, device=dev) if world > 1 and args.exchange == "p2p" else None
+    # --fused: the far read ends with the exchange (of one rank at N = 1) and the merge in one cooperative
+    # launch; otherwise the far read and the merge (or the peer exchange kernel) are two launches
+    fused = args.exchange == "p2p" and args.fused
+    peer = PeerExchange(n=B, hq=hq, hd=hd, device=dev) if args.exchange == "p2p" and (world > 1 or fused) else None
 
     def far(i):
         kernels.far_read(q_all[i], qsl, seq_all[i: i + 1], side, o_part, lse_part, window=W, block=B,
@@ -296,6 +302,11 @@ def run_gpu(args):
     def step(i):
         append(i)
         seq = seq_all[i: i + 1]
+        if fused:
+            kernels.far_read_exchange(peer.handle, q_all[i], qsl, seq, side, o_part, lse_part, o_l, lse_l, out,
+                                      window=W, block=B, far_distance=W + B, softmax_scale=hd ** -0.5, alpha=ALPHA,
+                                      table=table, pos_lo=pos_lo, capacity=length, err=err)
+            return
         far(i)
         if peer is not None:
             peer.merge(o_part, lse_part, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=ALPHA, err=err)
@@ -384,6 +395,23 @@ def run_gpu(args):
     torch.cuda.synchronize()
     far_sustained_ms = f0.elapsed_time(f1) / args.steps
     del far_graph
+    fused_ms = None
+    if fused:  # the far read that ends with the merge (exchange) alone, timed as the far read above
+        fg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(fg):
+            for j in range(args.steps):
+                i = args.warmup + j
+                kernels.far_read_exchange(peer.handle, q_all[i], qsl, seq_all[i: i + 1], side, o_part, lse_part, o_l,
+                                          lse_l, out, window=W, block=B, far_distance=W + B, softmax_scale=hd ** -0.5,
+                                          alpha=ALPHA, table=table, pos_lo=pos_lo, capacity=length, err=err)
+        fg.replay()
+        torch.cuda.synchronize()
+        f0.record(stream)
+        fg.replay()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        fused_ms = f0.elapsed_time(f1) / args.steps
+        del fg
     window = run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err,
                         append) if world == 1 else None
     # every rank takes part in the reduction before any rank may raise (same collectives everywhere)
@@ -406,7 +434,8 @@ def run_gpu(args):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local)
+        e2e = run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local,
+                      peer if fused else None)
 
     if rank == 0:
         line = {
@@ -425,9 +454,15 @@ def run_gpu(args):
             "config": {"workload": cfg["name"], "context": cfg["ctx"], "window": W, "block": B, "heads_q": hq,
                        "heads_kv": hkv, "head_dim": hd, "alpha": ALPHA, "splits": splits,
                        "parallelism": f"seq-shard{world}" if world > 1 else "single",
+                       "step_kernels": ("append + far read ending with the merge in one cooperative kernel" if fused
+                                        and world == 1 else "append + far read ending with the peer exchange and the "
+                                        "merge in one cooperative kernel" if fused else "append + far read + merge"
+                                        if world == 1 else "append + far read + peer exchange kernel"
+                                        if peer is not None else "append + far read + combine + NCCL all-gather + "
+                                        "merge"),
                        "exchange": None if world == 1 else (
-                           "peer-to-peer kernel (NVLink stores + flags, combine and merge fused)" if peer is not None
-                           else "combine + NCCL all-gather + merge"),
+                           "peer-to-peer (NVLink stores of self-validating lines, combine and merge fused)"
+                           if peer is not None else "NCCL all-gather"),
                        "timing": "eager launches" if args.eager else "CUDA graph of the K timed steps",
                        "l2": "inputs larger than L2 (side cache %.0f MB per GPU)" % (side.numel() * 2 / 1e6)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -435,8 +470,9 @@ def run_gpu(args):
                          "kernel": "far_read_kernel", "kernel_us": round(far_ms * 1000, 3),
                          "kernel_timing": "burst: the far read alone, one graph of K launches after idle",
                          "kernel_us_sustained": round(far_sustained_ms * 1000, 3),
+                         "fused_kernel_us": None if fused_ms is None else round(fused_ms * 1000, 3),
                          "algorithmic_bytes": int(alg), "traffic": traffic},
-            "gpu_launches": args.steps * (3 if world == 1 or peer is not None else 4),
+            "gpu_launches": args.steps * (2 if fused else 3 if world == 1 or peer is not None else 4),
             "clocks": clocks.summary(),
             "e2e": e2e,
         }
@@ -533,13 +569,20 @@ def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_
                          "of K steps, sustained"}
 
 
-def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local):
-    """The same steps through the public workspace API with pinned host inputs: per step the
-    query, the accepted K/V and their positions are copied host->device inside the timed region,
-    and the merged output is read back device->host."""
+def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local, peer):
+    """The same steps through the public workspace API with pinned host inputs. Per step, the
+    query, the K/V, positions and slots of the tokens the previous step accepted, and seq_len are
+    copied host->device inside the timed region, and the merged output is read back device->host.
+
+    The layer's calls (FoldWorkspace.append, read_far or ShardedFarMemory.step, the merge) are
+    captured once in a CUDA graph per input buffer, as vLLM captures the drafter's forward, and
+    replayed per step. A step's record has room for B accepted tokens. Rows past the accepted
+    count carry slot -1, which the append sends to the dummy slot (fold/attention.py:262), so one
+    graph serves every acceptance count."""
     import torch
     import torch.distributed as dist
 
+    from fold_b200 import kernels
     from fold_b200.attention import FoldWorkspace
     from fold_b200.shard import ShardedFarMemory, ShardPlan
 
@@ -552,51 +595,79 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
                        shard_len=plan.held if world > 1 else None)
     ws.side = side  # the same resident side cache as the kernel leg
     ws._table = table
-    sharded = ShardedFarMemory(plan, ws, exchange=args.exchange) if world > 1 else None
+    ws.partials(B, hq)  # allocated before capture
+    sharded = ShardedFarMemory(plan, ws, exchange=args.exchange, peer=peer) if world > 1 else None
     gen = torch.Generator().manual_seed(args.seed + 99)
-    max_acc = int(acc.max())
-    # One pinned record per step, uploaded with one copy: the step's query, the K/V and positions
-    # of the tokens the previous step accepted, and the step's seq_len (every field 8-byte aligned).
+    max_acc = B
+    # One pinned record per step, uploaded with one copy: the step's query, the K/V, positions and
+    # slots of the tokens the previous step accepted, and the step's seq_len (fields 16-byte aligned).
     qb, kb = B * hq * hd * 2, max_acc * hkv * hd * 2
     off_k, off_v, off_pos = qb, qb + kb, qb + 2 * kb
-    off_seq = off_pos + max_acc * 8
+    off_slot = off_pos + max_acc * 8
+    off_seq = off_slot + max_acc * 8
     rec = (off_seq + 4 + 15) // 16 * 16
     h_in = torch.zeros((total, rec), dtype=torch.uint8)
     for i in range(total):
         h_in[i, :qb].view(torch.bfloat16).copy_(torch.randn(B * hq * hd, generator=gen))
-        if i > 0:
-            a = int(acc[i - 1])
+        a = int(acc[i - 1]) if i > 0 else 0
+        if a:
             h_in[i, off_k:off_k + a * hkv * hd * 2].view(torch.bfloat16).copy_(torch.randn(a * hkv * hd, generator=gen))
             h_in[i, off_v:off_v + a * hkv * hd * 2].view(torch.bfloat16).copy_(torch.randn(a * hkv * hd, generator=gen))
-            h_in[i, off_pos:off_pos + a * 8].view(torch.int64).copy_(torch.arange(int(H[i - 1]), int(H[i - 1]) + a))
+        pos = torch.full((max_acc,), -1, dtype=torch.int64)
+        if a:
+            pos[:a] = torch.arange(int(H[i - 1]), int(H[i - 1]) + a)
+        h_in[i, off_pos:off_pos + max_acc * 8].view(torch.int64).copy_(pos.clamp_min(0))
+        h_in[i, off_slot:off_slot + max_acc * 8].view(torch.int64).copy_(pos)
         h_in[i, off_seq:off_seq + 4].view(torch.int32).fill_(int(H[i]) + B)
     h_in = h_in.pin_memory()
     h_out = torch.empty((2, B, hq, hd), dtype=torch.bfloat16).pin_memory()
     qsl = torch.tensor([0, B], dtype=torch.int32, device=dev)
     o_l = torch.randn((B, hq, hd), device=dev, dtype=torch.bfloat16)
     lse_l = torch.randn((hq, B), device=dev) + 5.0
-    from fold_b200 import kernels
     scale = hd ** -0.5
 
-    # Two input records and two outputs on the device: while step i computes on one, the upload of
-    # step i+1's inputs (its own stream) fills the other, and the read-back of step i-1's output
-    # (a third stream) drains the other output.
     class Slot:
+        """One device input record and output, with the captured step that reads and writes them."""
+
         def __init__(self):
-            self.d_in = torch.empty(rec, device=dev, dtype=torch.uint8)
+            self.d_in = torch.zeros(rec, device=dev, dtype=torch.uint8)
             d = self.d_in
             self.q = d[:qb].view(torch.bfloat16).view(B, hq, hd)
-            k = d[off_k:off_k + kb].view(torch.bfloat16).view(max_acc, hkv, hd)
-            v = d[off_v:off_v + kb].view(torch.bfloat16).view(max_acc, hkv, hd)
-            pos = d[off_pos:off_pos + max_acc * 8].view(torch.int64)
+            self.k = d[off_k:off_k + kb].view(torch.bfloat16).view(max_acc, hkv, hd)
+            self.v = d[off_v:off_v + kb].view(torch.bfloat16).view(max_acc, hkv, hd)
+            self.pos = d[off_pos:off_pos + max_acc * 8].view(torch.int64)
+            self.slots = d[off_slot:off_slot + max_acc * 8].view(torch.int64)
             self.seq = d[off_seq:off_seq + 4].view(torch.int32)
-            self.accepted = {a: (k[:a], v[:a], pos[:a]) for a in range(1, max_acc + 1)}
             self.out = torch.empty((B, hq, hd), device=dev, dtype=torch.bfloat16)
             self.uploaded, self.computed, self.read = (torch.cuda.Event() for _ in range(3))
+            self.graph = None
+
+        def layer_step(self):
+            ws.append(self.k, self.v, self.pos, self.slots)
+            if peer is not None and sharded is None:
+                peer.read_merge(ws, self.q, qsl, self.seq, scale, o_l, lse_l, self.out)
+            elif sharded is not None and peer is not None:
+                sharded.step_merge(self.q, qsl, self.seq, scale, o_l, lse_l, self.out, fused=True)
+            elif sharded is not None:
+                o_all, lse_all = sharded.step(self.q, qsl, self.seq, scale)
+                sharded.merge(o_l, lse_l, o_all, lse_all, self.out, qsl, self.seq)
+            else:
+                o_part, lse_part = ws.read_far(self.q, qsl, self.seq, scale)
+                kernels.merge(o_l, lse_l, o_part, lse_part, self.out, qsl, self.seq, window=W, block=B, alpha=ALPHA)
 
     slots = (Slot(), Slot())
     compute = torch.cuda.current_stream(dev)
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    # capture after one eager run of each (every rank captures the same collectives in the same order)
+    for sl in slots:
+        sl.d_in.copy_(h_in[0])
+        sl.layer_step()
+    torch.cuda.synchronize()
+    for sl in slots:
+        sl.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(sl.graph):
+            sl.layer_step()
+    torch.cuda.synchronize()
 
     def upload(i):
         sl = slots[i % 2]
@@ -611,16 +682,7 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
         compute.wait_event(sl.uploaded)
         if i >= 2:
             compute.wait_event(sl.read)  # step i-2's output has been read back
-        a = int(acc[i - 1]) if i > 0 else 0
-        if a:
-            k, v, pos = sl.accepted[a]
-            ws.append(k, v, pos, pos)
-        if sharded is not None:
-            o_all, lse_all = sharded.step(sl.q, qsl, sl.seq, scale)
-            sharded.merge(o_l, lse_l, o_all, lse_all, sl.out, qsl, sl.seq)
-        else:
-            o_part, lse_part = ws.read_far(sl.q, qsl, sl.seq, scale)
-            kernels.merge(o_l, lse_l, o_part, lse_part, sl.out, qsl, sl.seq, window=W, block=B, alpha=ALPHA)
+        sl.graph.replay()
         sl.computed.record(compute)
         if i + 1 < last:
             upload(i + 1)
@@ -637,6 +699,17 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
 
     run(0, args.warmup)
     torch.cuda.synchronize()
+    # untimed passes over the timed steps first, so that the timed region runs under the same
+    # sustained load (and power-capped clock) as the device-timed step; the count is rank 0's
+    t0 = time.perf_counter()
+    run(args.warmup, total)
+    torch.cuda.synchronize()
+    pre = torch.tensor([max(0, min(20, int(0.3 / max(time.perf_counter() - t0, 1e-4))))], device=dev)
+    if world > 1:
+        dist.broadcast(pre, src=0)
+    for _ in range(int(pre.item())):
+        run(args.warmup, total)
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -647,15 +720,21 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    if sharded is not None and sharded.peer is not None:
+    for sl in slots:
+        sl.graph = None  # graphs that hold collectives go before the process group
+    torch.cuda.synchronize()
+    if sharded is not None and sharded.peer is not None and sharded.peer is not peer:
         sharded.peer.close()
     return {"value": round(1000.0 * float(ms) / args.steps, 3), "unit": "us/draft-step",
             "h2d_bytes_per_step": rec, "d2h_bytes_per_step": B * hq * hd * 2,
-            "api": ("FoldWorkspace.append/read_far + " + ("ShardedFarMemory step/merge" if sharded is not None
-                                                           else "kernels.merge") + " (fold_b200 C-ABI), eager "
-                    "launches; per step one pinned host->device copy of the step's inputs and one device->host copy "
-                    "of its output, each on its own stream, double-buffered so that they overlap the neighbouring "
-                    "steps' kernels")}
+            "api": ("FoldWorkspace.append + " + (
+                "PeerExchange.read_merge (far read + merge in one cooperative kernel)" if peer is not None and
+                sharded is None else "ShardedFarMemory.step_merge (far read + peer exchange + merge in one "
+                "cooperative kernel)" if peer is not None else "ShardedFarMemory step/merge" if sharded is not None
+                else "FoldWorkspace.read_far + kernels.merge") + " (fold_b200 C-ABI), captured "
+                    "once per input buffer in a CUDA graph and replayed per step; per step one pinned host->device "
+                    "copy of the step's inputs and one device->host copy of its output, each on its own stream, "
+                    "double-buffered so that they overlap the neighbouring steps")}
 
 
 # ------------------------------------------------------------------------------ reference arm

@@ -46,6 +46,9 @@ SIGNATURES = {
     "fold_exchange_destroy": [_vp],
     "fold_exchange_merge": [_vp, _vp, _vp, _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32,
                             _i32, _i32, _i32, _i32, _f32, _vp, _vp],
+    "fold_far_read_exchange": [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp, _vp,
+                               _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
+                               _i32, _i32, _f32, _f32, _vp, _vp],
     "fold_far_read_merge_static": [_vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp, _i64,
                                    _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                    _i32, _f32, _f32, _vp, _vp],

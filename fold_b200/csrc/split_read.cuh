@@ -1,0 +1,689 @@
+#pragma once
+
+// The split-KV read of FOLD (fold/attention.py:162-170 of the reference) as a device template:
+// one CTA per (split, KV head) streams tiles of keys with TMA and computes the split's partial
+// (o, lse) on mma.sync tiles. far_read.cu instantiates it as the far-memory read (side cache,
+// query rotated to the shared far position) and as the window read (paged drafter cache, exact
+// positions); far_exchange.cu adds the exchange of the partials after it.
+//
+// Per CTA: thread 0 keeps a ring of shared-memory stages filled with tiles of TK keys of this
+// head's K and V rows (TMA, 128-byte swizzle, completion on mbarriers), and all eight warps
+// compute, per tile,
+//   S^T = K . Qf^T     (keys on the MMA M dimension, the n*G query rows on N: no row padding)
+//   P^T = exp2(S^T * scale * log2e - m)      (online softmax with a lazily raised row maximum)
+//   O^T += V^T . P^T
+// on bf16 mma.sync tiles, and finally write the split's normalised partial (o, lse).
+//
+// The running row maximum m only moves when a new logit exceeds it by more than kRaise (log2
+// units), which is decided for the whole CTA by one OR-barrier per tile. So the common tile needs
+// no cross-warp max exchange and no rescaling. P stays below 2^kRaise: bf16 keeps its 8-bit
+// mantissa at any magnitude and the fp32 sums of at most 2^16 * (keys per split) stay far from
+// overflow, so a high threshold costs no accuracy and makes raises rare after the first tile.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "far_read.cuh"
+
+namespace fold {
+
+template <int HD_, int NT_, int TK_, int HG_>
+struct FarCfg {
+  static constexpr int HD = HD_, NT = NT_, TK = TK_, HG = HG_;
+  static constexpr int ROWS = 8 * NT;
+  static constexpr int NW = 8;  // warps; thread 0 also issues the TMA copies
+  static constexpr int NTHREADS = NW * 32;
+  static constexpr int KBOX = HD / 64;  // 64-column boxes per K (and per V) row block
+  static constexpr int BOX_BYTES = TK * 128;
+  static constexpr int STAGE_BYTES = 2 * KBOX * BOX_BYTES;
+  static constexpr int MT = TK / 16;  // key m-tiles per tile (one per QK warp column)
+  static constexpr int NG = NW / MT;  // QK warps sharing one m-tile split the n-tiles
+  static constexpr int QNT = (NT + NG - 1) / NG;
+  static constexpr int KG = NW / HG;  // PV: HG hd groups x KG key groups
+  static constexpr int PV_MT = HD / 16 / HG;
+  static constexpr int PV_KS = TK / 16 / KG;
+  static constexpr int QSTRIDE = HD + 8;                        // elements; 16-byte units odd
+  static constexpr int PSTRIDE = 8 * ((NT & 1) ? NT : NT + 1);  // elements; 16-byte units odd
+  static constexpr bool Q_REGS = QNT * (HD / 16) * 2 <= 80;
+  static constexpr int Q_BYTES = ROWS * QSTRIDE * 2;
+  static constexpr int P_BYTES = 2 * TK * PSTRIDE * 2;
+  static constexpr int RED_BYTES = MT * ROWS * 4;
+  static constexpr int ROW_BYTES = 2 * 64 * 4;
+  static constexpr int FIXED = Q_BYTES + P_BYTES + RED_BYTES + ROW_BYTES + 8 * 8 + 1024;
+  static constexpr int NSTAGE_FIT = (kSmemLimit - FIXED) / STAGE_BYTES;
+  static constexpr int NSTAGE = NSTAGE_FIT > 4 ? 4 : NSTAGE_FIT;
+  static constexpr int OFF_Q = NSTAGE * STAGE_BYTES;
+  static constexpr int OFF_P = OFF_Q + Q_BYTES;
+  static constexpr int OFF_RED = OFF_P + P_BYTES;
+  static constexpr int OFF_ROW = OFF_RED + RED_BYTES;
+  static constexpr int OFF_BAR = OFF_ROW + ROW_BYTES;
+  static constexpr int SMEM = OFF_BAR + 8 * 8 + 1024;
+  static_assert(NSTAGE >= 2, "shared memory too small for two stages");
+  static_assert(SMEM <= kSmemLimit, "shared memory budget");
+  static_assert(MT * NG == NW && HG * KG == NW, "warp split");
+  static_assert(PV_MT >= 1 && PV_KS >= 1, "warp split");
+  static_assert(ROWS * HD * 4 <= NSTAGE * STAGE_BYTES, "epilogue staging");
+  static_assert(TK <= 256 && 256 % TK == 0, "tiles stay inside one 256-entry page");
+};
+
+
+// Issues the TMA copies of tile `tile` (index in this cache) of head h into stage `st`.
+template <class C>
+__device__ __forceinline__ void issue_tile(unsigned char* smem, uint64_t* full, const CUtensorMap* map, int st,
+                                           int tile, int hkv, int h, uint64_t pol) {
+  mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+  const int64_t lp = static_cast<int64_t>(tile) * C::TK;
+  const int page = static_cast<int>(lp >> 8), off = static_cast<int>(lp & 255);
+  const int c2 = page * hkv + h;
+  unsigned char* dst = smem + st * C::STAGE_BYTES;
+#pragma unroll
+  for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
+}
+
+// Window read: issues the copies of the tile of positions [tpos, tpos + TK) of head h from the
+// paged cache into stage `st`, in 16-position chunks (every block size is a multiple of 16, so a
+// chunk never straddles two blocks). Each chunk lands where a TK-row box would have put it, so
+// the stage has the far read's layout. Chunks past the last context entry reload the last valid
+// chunk (the consumers zero those V rows and mask those keys); a block-table entry outside the
+// cache records FOLD_DEVERR_BLOCK_TABLE and reads block 0 instead.
+template <class C>
+__device__ __forceinline__ void issue_window_tile(unsigned char* smem, uint64_t* full, const CUtensorMap* kmap,
+                                                  const CUtensorMap* vmap, int st, int64_t tpos, int seq, int h,
+                                                  const FarParams& p, uint64_t pol) {
+  constexpr int CH = C::TK / 16;
+  const int64_t last = (static_cast<int64_t>(seq - 1) / 16) * 16;  // a tile exists only when seq >= 1
+  int blk[CH], slot[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {  // all table loads first: one latency for the whole tile
+    const int64_t pos = min64(tpos + 16 * c, last);
+    const int lb = static_cast<int>(pos / p.block_size);
+    slot[c] = static_cast<int>(pos - static_cast<int64_t>(lb) * p.block_size);
+    blk[c] = lb < p.bt_len ? __ldg(p.block_table + lb) : -1;
+  }
+  mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+  unsigned char* dst = smem + st * C::STAGE_BYTES;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    int b = blk[c];
+    if (b < 0 || b >= p.num_blocks) {
+      set_error(p.err, FOLD_DEVERR_BLOCK_TABLE);
+      b = 0;
+    }
+    const int c1 = p.head_inner ? h : slot[c], c2 = p.head_inner ? slot[c] : h;
+#pragma unroll
+    for (int x = 0; x < C::KBOX; ++x) {
+      tma_load_4d(dst + x * C::BOX_BYTES + c * 2048, kmap, &full[st], x * 64, c1, c2, b, pol);
+      tma_load_4d(dst + (C::KBOX + x) * C::BOX_BYTES + c * 2048, vmap, &full[st], x * 64, c1, c2, b, pol);
+    }
+  }
+}
+
+// One thread's share of a CTA's query rows for the vectorised rotation: each work item is one
+// row's pair of 8-element chunks ([8c, 8c+8) with its neox partner [RH+8c, ...), or 16 unrotated
+// elements), held as 16-byte vectors. The loads are issued first thing in the kernel (they depend
+// on nothing the kernel reads), so their latency overlaps the step-length and table reads.
+template <class C>
+struct QueryLoad {
+  static constexpr int PAIRS = C::HD / 16;
+  static constexpr int ITEMS = C::ROWS * PAIRS;
+  static constexpr int MAXI = (ITEMS + C::NTHREADS - 1) / C::NTHREADS;
+  uint4 a[MAXI], b[MAXI];
+};
+
+// rh8 = rotated 8-element chunks per half (0: no rotation).
+template <class C>
+__device__ __forceinline__ void load_query_vec(const FarParams& p, int rh8, int RH, int h, int nrows, int G,
+                                               QueryLoad<C>& ql) {
+  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS;
+#pragma unroll
+  for (int k = 0; k < QueryLoad<C>::MAXI; ++k) {
+    const int e = threadIdx.x + k * C::NTHREADS;
+    ql.a[k] = ql.b[k] = make_uint4(0, 0, 0, 0);
+    if (e < ITEMS) {
+      const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
+      if (rho < nrows) {
+        const int r = rho / G, hq = h * G + (rho - r * G);
+        const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
+        const int off_a = c < rh8 ? 8 * c : 2 * RH * (rh8 > 0) + 16 * (c - rh8);
+        const int off_b = c < rh8 ? RH + 8 * c : off_a + 8;
+        ql.a[k] = __ldg(reinterpret_cast<const uint4*>(qr + off_a));
+        ql.b[k] = __ldg(reinterpret_cast<const uint4*>(qr + off_b));
+      }
+    }
+  }
+}
+
+// Vectorised far-query rotation of the loaded rows with the table row `trow` (cos then sin; read
+// only when rh8 > 0), written to the query tile Qs (and to qf by split 0). Every thread issues its
+// table loads before any arithmetic, so this costs one memory latency.
+template <class C>
+__device__ __forceinline__ void rotate_query_vec(const FarParams& p, const QueryLoad<C>& ql, const float* trow,
+                                                 int rh8, int RH, float sgn, int h, int split, int nrows, int G,
+                                                 __nv_bfloat16* Qs) {
+  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS, MAXI = QueryLoad<C>::MAXI;
+  const int tid = threadIdx.x;
+  float4 c0[MAXI], c1[MAXI], s0[MAXI], s1[MAXI];
+#pragma unroll
+  for (int k = 0; k < MAXI; ++k) {
+    const int e = tid + k * C::NTHREADS;
+    c0[k] = c1[k] = s0[k] = s1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < ITEMS) {
+      const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
+      if (rho < nrows && c < rh8) {
+        const float4* tc = reinterpret_cast<const float4*>(trow + 8 * c);
+        const float4* ts = reinterpret_cast<const float4*>(trow + RH + 8 * c);
+        c0[k] = __ldg(tc), c1[k] = __ldg(tc + 1), s0[k] = __ldg(ts), s1[k] = __ldg(ts + 1);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < MAXI; ++k) {
+    const int e = tid + k * C::NTHREADS;
+    if (e >= ITEMS) continue;
+    const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
+    int off_a, off_b;
+    uint4 ya = ql.a[k], yb = ql.b[k];
+    if (c < rh8) {
+      off_a = 8 * c, off_b = RH + 8 * c;
+      const float cs[8] = {c0[k].x, c0[k].y, c0[k].z, c0[k].w, c1[k].x, c1[k].y, c1[k].z, c1[k].w};
+      const float sn[8] = {s0[k].x, s0[k].y, s0[k].z, s0[k].w, s1[k].x, s1[k].y, s1[k].z, s1[k].w};
+      const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&ql.a[k]);
+      const __nv_bfloat162* xb = reinterpret_cast<const __nv_bfloat162*>(&ql.b[k]);
+      uint32_t* oa = reinterpret_cast<uint32_t*>(&ya);
+      uint32_t* ob = reinterpret_cast<uint32_t*>(&yb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = __bfloat1622float2(xa[j]), xp = __bfloat1622float2(xb[j]);
+        const float c_0 = cs[2 * j], c_1 = cs[2 * j + 1];
+        const float s_0 = sgn * sn[2 * j], s_1 = sgn * sn[2 * j + 1];
+        oa[j] = pack_bf16(x.x * c_0 - xp.x * s_0, x.y * c_1 - xp.y * s_1);
+        ob[j] = pack_bf16(xp.x * c_0 + x.x * s_0, xp.y * c_1 + x.y * s_1);
+      }
+    } else {
+      off_a = 2 * RH * (rh8 > 0) + 16 * (c - rh8), off_b = off_a + 8;
+    }
+    *reinterpret_cast<uint4*>(Qs + rho * C::QSTRIDE + off_a) = ya;
+    *reinterpret_cast<uint4*>(Qs + rho * C::QSTRIDE + off_b) = yb;
+    if (p.qf && split == 0 && rho < nrows) {
+      const int r = rho / G, hq = h * G + (rho - r * G);
+      __nv_bfloat16* o = p.qf + r * p.qf_st + hq * p.qf_sh;
+      *reinterpret_cast<uint4*>(o + off_a) = ya;
+      *reinterpret_cast<uint4*>(o + off_b) = yb;
+    }
+  }
+}
+
+// Window read: first and one-past-last visible position of row r (at position hist + r) under the
+// FlashAttention window [p - left, p + right] (a negative side is unbounded), causal or not,
+// within the seq context entries. Both grow with r.
+__device__ __forceinline__ int64_t window_lo(const FarParams& p, int hist, int r) {
+  return p.win_left < 0 ? 0 : max64(0, static_cast<int64_t>(hist) + r - p.win_left);
+}
+__device__ __forceinline__ int64_t window_hi(const FarParams& p, int hist, int seq, int r) {
+  const int64_t pos = static_cast<int64_t>(hist) + r;
+  int64_t hi = seq;
+  if (p.win_right >= 0) hi = min64(hi, pos + p.win_right + 1);
+  if (p.causal) hi = min64(hi, pos + 1);
+  return max64(hi, 0);
+}
+
+// Zeroes the V rows [from, TK) of a landed stage (window read: positions past the context, whose
+// cache slots may hold anything; their P is 0, but 0 * NaN would not be).
+template <class C>
+__device__ __forceinline__ void zero_v_rows(unsigned char* stage, int from) {
+  const int per_box = (C::TK - from) * 8;  // 16-byte units
+  for (int u = threadIdx.x; u < per_box * C::KBOX; u += C::NTHREADS) {
+    const int x = u / per_box, r = u - x * per_box;
+    *reinterpret_cast<uint4*>(stage + (C::KBOX + x) * C::BOX_BYTES + (from + (r >> 3)) * 128 + (r & 7) * 16) =
+        make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_shared();  // the stage is refilled by TMA later
+}
+
+// The split-KV read of one (split, KV head), in two modes.
+//   WIN = false, far memory: K|V rows of the side cache through `map`, the query rotated to the
+//     shared far position, row r reads positions [0, H - W - B + 1 + r) (fold/attention.py:164).
+//   WIN = true, window read: K through `map` and V through `vmap` from the paged cache, the
+//     query as given, row r reads its exact-position window (fold/attention.py:148-151,163).
+template <class C, bool WIN>
+__device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
+                                           int split) {
+  constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
+  constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_Q);
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  float* row_m = reinterpret_cast<float*>(smem + C::OFF_ROW);
+  float* row_inv = row_m + 64;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.y;
+  const int G = p.group;
+  const int nrows = p.n * G;
+  const int RH = p.rot_dim >> 1;
+  const int rh8 = (!WIN && p.table) ? RH / 8 : 0;  // the far read rotates when it has a table
+  QueryLoad<C> ql;
+  if (p.vec_rot) load_query_vec<C>(p, rh8, RH, h, nrows, G, ql);
+
+  // Step geometry, from the device-side lengths (fold/kernels.py:24-30).
+  const int qlen = p.qsl[1] - p.qsl[0];
+  const int seq = p.seq[0];
+  const int hist = max(seq - qlen, 0);
+  int lim_base = 0;  // far: row r reads positions [0, lim_base + r)
+  int64_t end;       // far: end of this cache's keys for the last row
+  int64_t pos0;      // position of tile 0
+  int tiles;
+  if constexpr (!WIN) {
+    lim_base = hist - p.window - p.block + 1;
+    end = min64(max(lim_base + p.n - 1, 0), p.pos_lo + p.local_cap);
+    const int64_t len = max64(end - p.pos_lo, 0);
+    tiles = static_cast<int>((len + TK - 1) / TK);
+    pos0 = p.pos_lo;
+  } else {
+    const int64_t u_lo = window_lo(p, hist, 0), u_hi = window_hi(p, hist, seq, p.n - 1);
+    const int64_t t0 = u_lo / TK;
+    tiles = u_hi > u_lo ? static_cast<int>((u_hi + TK - 1) / TK - t0) : 0;
+    pos0 = t0 * TK;
+    end = u_hi;
+  }
+  const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / p.splits);
+  const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / p.splits) - t_begin;
+
+  uint64_t pol = 0;
+  auto issue = [&](int st, int t) {  // tile t of this cache into stage st
+    if constexpr (WIN)
+      issue_window_tile<C>(smem, full, map, vmap, st, pos0 + static_cast<int64_t>(t) * TK, seq, h, p, pol);
+    else
+      issue_tile<C>(smem, full, map, st, t, p.hkv, h, pol);
+  };
+  if (tid == 0) {
+    if constexpr (!WIN) {
+      if (split == 0 && h == 0) {
+        const int far_len = max(hist - p.window - p.block + qlen, 0);
+        if (p.far_len) *p.far_len = far_len;
+        if (far_len > p.capacity) set_error(p.err, FOLD_DEVERR_CAPACITY);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NSTAGE; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    // Fill the ring right away, so the first copies overlap the query rotation below.
+    pol = l2_evict_first_policy();
+    prefetch_tensormap(map);
+    if constexpr (WIN) prefetch_tensormap(vmap);
+    for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
+  }
+
+  // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table.
+  // The window read takes the query as it is.
+  {
+    const float* trow = nullptr;
+    float sgn = 1.f;
+    if constexpr (!WIN) {
+      const int delta = p.far_distance - hist;
+      int ad = delta < 0 ? -delta : delta;
+      sgn = delta < 0 ? -1.f : 1.f;
+      if (p.table && ad >= p.table_rows) {
+        if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
+        ad = p.table_rows - 1;
+      }
+      trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
+    }
+    if (p.vec_rot) {
+      rotate_query_vec<C>(p, ql, trow, rh8, RH, sgn, h, split, nrows, G, Qs);
+    } else {
+      for (int e = tid; e < ROWS * HD; e += NTH) {
+        const int rho = e / HD, d = e - (e / HD) * HD;
+        float y = 0.f;
+        if (rho < nrows) {
+          const int r = rho / G, hq = h * G + (rho - r * G);
+          const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
+          const float x = bf2f(qr[d]);
+          if (trow && d < 2 * RH) {
+            const bool lo = d < RH;
+            const int i = lo ? d : d - RH;
+            const float xp = bf2f(qr[lo ? d + RH : d - RH]);
+            const float c = trow[i], s = sgn * trow[RH + i];
+            y = lo ? x * c - xp * s : x * c + xp * s;
+          } else {
+            y = x;
+          }
+          const __nv_bfloat16 yb = __float2bfloat16_rn(y);
+          if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
+          Qs[rho * C::QSTRIDE + d] = yb;
+        } else {
+          Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);
+        }
+      }
+    }
+  }
+  __syncthreads();  // barrier inits and the query tile are visible to every warp
+
+  // Warp roles.
+  const int mt = warp % MT, ng = warp / MT, nt_lo = ng * QNT;  // QK: key m-tile, n-tile group
+  const int hg = warp % C::HG, kg = warp / C::HG;                 // PV: hd group, key group
+  const int g4 = lane >> 2, t4 = lane & 3;
+
+  // Query fragments (B operand of S^T = K . Q^T) for this warp's n-tiles.
+  uint32_t qfr[C::Q_REGS ? QNT : 1][C::Q_REGS ? HD / 16 : 1][2];
+  const uint32_t qs_base = smem_u32(Qs);
+  if constexpr (C::Q_REGS) {
+#pragma unroll
+    for (int j = 0; j < QNT; ++j) {
+      const int nt = min(nt_lo + j, NT - 1);
+#pragma unroll
+      for (int kp = 0; kp < HD / 32; ++kp) {
+        const uint32_t a = qs_base + ((nt * 8 + (lane & 7)) * C::QSTRIDE + kp * 32 + (lane >> 3) * 8) * 2;
+        ldsm_x4(a, qfr[j][2 * kp][0], qfr[j][2 * kp][1], qfr[j][2 * kp + 1][0], qfr[j][2 * kp + 1][1]);
+      }
+    }
+  }
+
+  // Row limits of this thread's QK rows (global positions; 0 for padding rows): keys
+  // [llo, lim) are visible, llo being 0 for the far read.
+  int lim[QNT][2];
+  int llo[WIN ? QNT : 1][2];
+#pragma unroll
+  for (int j = 0; j < QNT; ++j)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int rho = (nt_lo + j) * 8 + t4 * 2 + c;
+      const bool valid = rho < nrows && nt_lo + j < NT;
+      if constexpr (WIN) {
+        lim[j][c] = valid ? static_cast<int>(window_hi(p, hist, seq, rho / G)) : 0;
+        llo[j][c] = valid ? static_cast<int>(window_lo(p, hist, rho / G)) : 0;
+      } else {
+        lim[j][c] = valid ? static_cast<int>(min64(lim_base + rho / G, end)) : 0;
+      }
+    }
+
+  float oacc[PV_MT][NT][4];
+#pragma unroll
+  for (int a = 0; a < PV_MT; ++a)
+#pragma unroll
+    for (int b = 0; b < NT; ++b) oacc[a][b][0] = oacc[a][b][1] = oacc[a][b][2] = oacc[a][b][3] = 0.f;
+  // Row maxima (log2 domain) of all rows this thread touches in PV; with NG > 1 the QK rows are a
+  // subset kept separately (same values, computed from the same shared data).
+  float mrow[NT][2], mq_own[NG == 1 ? 1 : QNT][2], lq[QNT][2];
+#pragma unroll
+  for (int b = 0; b < NT; ++b) mrow[b][0] = mrow[b][1] = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < (NG == 1 ? 1 : QNT); ++j) mq_own[j][0] = mq_own[j][1] = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < QNT; ++j) lq[j][0] = lq[j][1] = 0.f;
+  auto MQ = [&](int j, int c) -> float& {
+    if constexpr (NG == 1) return mrow[j][c];
+    else return mq_own[j][c];
+  };
+
+  bool timed_out = false;
+  int consumed = 0;
+  const uint32_t p_base = smem_u32(smem + C::OFF_P);
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int st = it % NSTAGE;
+    const bool ok = mbar_wait(&full[st], (it / NSTAGE) & 1);
+    const uint32_t kv_base = smem_u32(smem + st * C::STAGE_BYTES);
+    const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
+    const int64_t tpos = pos0 + static_cast<int64_t>(t_begin + it) * TK;  // first position of the tile
+    const int64_t key0 = tpos + mt * 16 + g4;
+    if constexpr (WIN) {
+      const int valid = static_cast<int>(max64(0, min64(TK, seq - tpos)));
+      if (ok && valid < TK) zero_v_rows<C>(smem + st * C::STAGE_BYTES, valid);
+    }
+
+    float x[QNT][4];
+    float ls[QNT][2];
+    bool exceed = false;
+#pragma unroll
+    for (int j = 0; j < QNT; ++j) x[j][0] = x[j][1] = x[j][2] = x[j][3] = 0.f, ls[j][0] = ls[j][1] = 0.f;
+    if (ok) {
+      // ---- S^T = K . Q^T for keys [mt*16, mt*16+16) of the tile
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const int row = mt * 16 + (lane & 15);
+        const int chunk = (kk & 3) * 2 + (lane >> 4);
+        const uint32_t a = kv_base + (kk >> 2) * C::BOX_BYTES + row * 128 + ((chunk ^ (row & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(a, a0, a1, a2, a3);
+#pragma unroll
+        for (int j = 0; j < QNT; ++j) {
+          if (nt_lo + j < NT) {
+            uint32_t b0, b1;
+            if constexpr (C::Q_REGS) {
+              b0 = qfr[j][kk][0];
+              b1 = qfr[j][kk][1];
+            } else {
+              const uint32_t qa =
+                  qs_base + (((nt_lo + j) * 8 + (lane & 7)) * C::QSTRIDE + kk * 16 + ((lane >> 3) & 1) * 8) * 2;
+              ldsm_x2(qa, b0, b1);
+            }
+            mma_bf16(x[j], a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+      // ---- scale, mask, exponentiate against the current row maximum
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = e & 1;
+          const int64_t key = key0 + (e >> 1) * 8;
+          bool vis = key < lim[j][c];
+          if constexpr (WIN) vis = vis && key >= llo[j][c];
+          const float v = vis ? x[j][e] * p.scale_log2 : -INFINITY;
+          x[j][e] = v;
+          exceed |= v > MQ(j, c) + kRaise;
+        }
+      }
+      if (it == 0) {
+        exceed = true;  // the first tile always sets the row maxima: skip the provisional P
+      } else {
+#pragma unroll
+        for (int j = 0; j < QNT; ++j) {
+          const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
+          const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
+          const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+          const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+          ls[j][0] = p0 + p2;
+          ls[j][1] = p1 + p3;
+          if (nt_lo + j < NT) {
+            const int r0 = (nt_lo + j) * 8 + t4 * 2;
+            const int k0 = mt * 16 + g4;
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2),
+                         "r"(pack_bf16(p2, p3)));
+          }
+        }
+      }
+    }
+
+    // One barrier per tile: P^T of every warp is written, every warp is done with the previous
+    // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
+    const bool attention = named_bar_or(exceed || !ok, 1, NTH);
+    if (tid == 0 && it >= 1 && it - 1 + NSTAGE < ntiles)
+      issue((it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE);
+    if (attention) {
+      if (named_bar_or(!ok, 2, NTH)) {
+        timed_out = true;
+        if (lane == 0) set_error(p.err, FOLD_DEVERR_TIMEOUT);
+        break;
+      }
+      // ---- raise the row maximum where a logit passed it by more than 2^kRaise
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v = fmaxf(x[j][c], x[j][c + 2]);
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+          if (lane < 4 && nt_lo + j < NT) red[mt * ROWS + (nt_lo + j) * 8 + lane * 2 + c] = v;
+        }
+      }
+      named_bar_sync(2, NTH);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int row = nt * 8 + t4 * 2 + c;
+          float tm = red[row];
+#pragma unroll
+          for (int q = 1; q < MT; ++q) tm = fmaxf(tm, red[q * ROWS + row]);
+          const float mo = mrow[nt][c];
+          const float mn = tm > mo + kRaise ? tm : mo;
+          const float f = mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
+          mrow[nt][c] = mn;
+#pragma unroll
+          for (int a = 0; a < PV_MT; ++a) {
+            oacc[a][nt][c] *= f;
+            oacc[a][nt][c + 2] *= f;
+          }
+          if constexpr (NG == 1) {
+            lq[nt][c] *= f;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < QNT; ++j) {
+        if constexpr (NG > 1) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int row = min(nt_lo + j, NT - 1) * 8 + t4 * 2 + c;
+            float tm = red[row];
+#pragma unroll
+            for (int q = 1; q < MT; ++q) tm = fmaxf(tm, red[q * ROWS + row]);
+            const float mo = mq_own[j][c];
+            const float mn = tm > mo + kRaise ? tm : mo;
+            lq[j][c] *= mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
+            mq_own[j][c] = mn;
+          }
+        }
+        const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
+        const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
+        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+        ls[j][0] = p0 + p2;
+        ls[j][1] = p1 + p3;
+        if (nt_lo + j < NT) {
+          const int r0 = (nt_lo + j) * 8 + t4 * 2;
+          const int k0 = mt * 16 + g4;
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p2, p3)));
+        }
+      }
+      named_bar_sync(2, NTH);
+    }
+#pragma unroll
+    for (int j = 0; j < QNT; ++j) lq[j][0] += ls[j][0], lq[j][1] += ls[j][1];
+
+    // ---- O^T += V^T . P^T over this warp's hd group and key group
+#pragma unroll
+    for (int ks = 0; ks < C::PV_KS; ++ks) {
+      const int kk = kg * C::PV_KS + ks;
+      uint32_t bfr[NT][2];
+#pragma unroll
+      for (int nt = 0; nt + 1 < NT; nt += 2) {
+        const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        const int col = (nt + (lane >> 4)) * 8;
+        ldsm_x4_t(pt + (key * C::PSTRIDE + col) * 2, bfr[nt][0], bfr[nt][1], bfr[nt + 1][0], bfr[nt + 1][1]);
+      }
+      if constexpr (NT & 1) {
+        const int key = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        ldsm_x2_t(pt + (key * C::PSTRIDE + (NT - 1) * 8) * 2, bfr[NT - 1][0], bfr[NT - 1][1]);
+      }
+#pragma unroll
+      for (int a = 0; a < PV_MT; ++a) {
+        const int ht = hg * PV_MT + a;
+        const int q = lane >> 3;
+        const int key_row = kk * 16 + (q >> 1) * 8 + (lane & 7);
+        const int chunk = (ht & 3) * 2 + (q & 1);
+        const uint32_t va =
+            kv_base + (C::KBOX + (ht >> 2)) * C::BOX_BYTES + key_row * 128 + ((chunk ^ (key_row & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(va, a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16(oacc[a][nt], a0, a1, a2, a3, bfr[nt][0], bfr[nt][1]);
+      }
+    }
+    consumed = it + 1;
+  }
+
+  // -------------------------------------------------------------- epilogue
+  const int64_t o_split = static_cast<int64_t>(split) * p.n * p.hq * HD;
+  const int64_t l_split = static_cast<int64_t>(split) * p.hq * p.n;
+  if (timed_out) {
+    // Copies still in flight must land before this CTA's shared memory is released.
+    if (tid == 0) {
+      const int issued = min(ntiles, max(consumed, 1) - 1 + NSTAGE);
+      for (int i = consumed; i < issued; ++i)
+        if (!mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1)) break;
+    }
+    for (int e = tid; e < nrows * HD; e += NTH) {
+      const int rho = e / HD, d = e - rho * HD;
+      const int r = rho / G, hq = h * G + (rho - r * G);
+      p.o_part[o_split + (static_cast<int64_t>(r) * p.hq + hq) * HD + d] = 0.f;
+      if (d == 0) p.lse_part[l_split + static_cast<int64_t>(hq) * p.n + r] = -INFINITY;
+    }
+    return;
+  }
+  // row sums: lanes sharing t4 hold the same rows
+#pragma unroll
+  for (int j = 0; j < QNT; ++j)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float v = lq[j][c];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (lane < 4 && nt_lo + j < NT) red[mt * ROWS + (nt_lo + j) * 8 + lane * 2 + c] = v;
+    }
+  if (warp == 0 && lane < 4) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) row_m[nt * 8 + lane * 2] = mrow[nt][0], row_m[nt * 8 + lane * 2 + 1] = mrow[nt][1];
+  }
+  // every copy has landed and been consumed: the stage memory holds the O reduction
+  float* ored = reinterpret_cast<float*>(smem);
+#pragma unroll
+  for (int kgi = 0; kgi < C::KG; ++kgi) {
+    __syncthreads();
+    if (kg == kgi) {
+#pragma unroll
+      for (int a = 0; a < PV_MT; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = (hg * PV_MT + a) * 16 + g4 + (e >> 1) * 8;
+            const int row = nt * 8 + t4 * 2 + (e & 1);
+            float* o = ored + row * HD + d;
+            *o = kgi == 0 ? oacc[a][nt][e] : *o + oacc[a][nt][e];
+          }
+    }
+  }
+  __syncthreads();
+  if (tid < ROWS) {
+    float L = 0.f;
+#pragma unroll
+    for (int q = 0; q < MT; ++q) L += red[q * ROWS + tid];
+    const float m = row_m[tid];
+    row_inv[tid] = L > 0.f ? 1.f / L : 0.f;
+    if (tid < nrows) {
+      const int r = tid / G, hq = h * G + (tid - r * G);
+      p.lse_part[l_split + static_cast<int64_t>(hq) * p.n + r] = L > 0.f ? (m + __log2f(L)) * kLn2 : -INFINITY;
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < nrows * (HD / 4); e += NTH) {
+    const int rho = e / (HD / 4), d4 = e - rho * (HD / 4);
+    const int r = rho / G, hq = h * G + (rho - r * G);
+    const float s = row_inv[rho];
+    float4 v = reinterpret_cast<const float4*>(ored + rho * HD)[d4];
+    v.x *= s, v.y *= s, v.z *= s, v.w *= s;
+    reinterpret_cast<float4*>(p.o_part + o_split + (static_cast<int64_t>(r) * p.hq + hq) * HD)[d4] = v;
+  }
+}
+
+}  // namespace fold

@@ -179,6 +179,32 @@ def far_read(q, qsl, seq_lens, side, o_part, lse_part, *, window, block, far_dis
               _stream(q))
 
 
+def far_read_exchange(exchange, q, qsl, seq_lens, side, o_part, lse_part, out_l, lse_l, out, *, window, block,
+                      far_distance, softmax_scale, alpha, table=None, rot_dim=None, far_len=None, pos_lo=0,
+                      capacity=None, err=None):
+    """far_read followed, in the same cooperative launch, by the exchange of the ranks' partials
+    and the merge with the window read (out_l [n, Hq, D] bf16, lse_l [Hq, n]) into out [n, Hq, D]
+    bf16; `exchange` is the handle of an open exchange (shard.PeerExchange; one rank: the far
+    read and the merge in one launch). o_part/lse_part are the far read's split buffers (scratch).
+    The far softmax scale is alpha * softmax_scale."""
+    _require_cuda(q, qsl, seq_lens, side, o_part, lse_part, out_l, lse_l, out, table, far_len, err)
+    _check_lengths(qsl, seq_lens)
+    n, hq, d = q.shape
+    splits = _check_partials(o_part, lse_part, n, hq, d, "far_read_exchange")
+    if tuple(out_l.shape) != (n, hq, d) or tuple(out.shape) != (n, hq, d):
+        raise FoldError("far_read_exchange: q, out_l and out shapes differ")
+    if out_l.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or lse_l.dtype != torch.float32:
+        raise FoldError("far_read_exchange: out_l and out must be bfloat16 and lse_l float32")
+    if out_l.stride(-1) != 1 or out.stride(-1) != 1:
+        raise FoldError("far_read_exchange: the head dimension must be contiguous")
+    q, side_args = _side_args(q, side, table, rot_dim, pos_lo, capacity, far_len)
+    _lib.call("fold_far_read_exchange", exchange, _p(q), q.stride(0), q.stride(1), _p(qsl), _p(seq_lens), *side_args,
+              _p(o_part), _p(lse_part), splits, _p(out_l), out_l.stride(0), out_l.stride(1), _p(lse_l),
+              lse_l.stride(0), lse_l.stride(1), _p(out), out.stride(0), out.stride(1), n, hq, side.shape[1], d,
+              int(window), int(block), int(far_distance), float(softmax_scale) * float(alpha), 1.0 / float(alpha),
+              _p(err), _stream(q))
+
+
 def paged_planes(kv_cache, head_dim):
     """K and V planes [num_blocks, Hkv, block_size, D] of vLLM's FlashAttention cache
     kv_cache[num_blocks, Hkv, block_size, 2 * D] (views, no copy)."""

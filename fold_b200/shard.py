@@ -192,6 +192,31 @@ class PeerExchange:
                   kernels._stream(out))
         return out
 
+    def read_merge(self, ws, q, qsl, seq_lens, scale, out_l, lse_l, out, *, rotate=True, err=None):
+        """The far read of this rank's chunk (ws.read_far) and merge() in one cooperative launch
+        (kernels.far_read_exchange): every CTA of the far read, once all splits of its KV head have
+        finished, combines, exchanges and merges a share of that head's items. With one rank it
+        is the far read and the merge in one launch. Writes out [n, Hq, D] (bf16)."""
+        if self._ptr is None:
+            raise FoldError("the exchange is closed")
+        n, hq, d = q.shape
+        if n > self.n or hq != self.hq or d != self.hd:
+            raise FoldError("far read + exchange: the step is larger than the exchange was created for")
+        o_part, lse_part = ws.partials(n, hq)
+        kernels.far_read_exchange(self._ptr, q, qsl, seq_lens, ws.side, o_part, lse_part, out_l, lse_l, out,
+                                  window=ws.window, block=ws.block, far_distance=ws.far_distance,
+                                  softmax_scale=scale, alpha=ws.alpha, table=ws.table if rotate else None,
+                                  far_len=ws.far_len, pos_lo=ws.pos_lo, capacity=ws.capacity,
+                                  err=ws.err if err is None else err)
+        return out
+
+    @property
+    def handle(self) -> int:
+        """The C-ABI handle of the exchange (for kernels.far_read_exchange)."""
+        if self._ptr is None:
+            raise FoldError("the exchange is closed")
+        return self._ptr
+
     def close(self):
         """Waits for this rank's work, meets the other ranks, then unmaps and frees the region."""
         if self._ptr is None:
@@ -247,6 +272,18 @@ class ShardedFarMemory:
         kernels.combine(o_part, lse_part, o, lse)  # writes straight into the send buffer
         dist.all_gather_into_tensor(recv, send, group=self.group)
         return unpack_partials(recv, self.plan.world, n, hq, d)
+
+    def step_merge(self, q, qsl, seq_lens, scale, out_l, lse_l, out, *, fused=False):
+        """step() and merge() of one draft step. fused=True (exchange="p2p" only) runs them as one
+        cooperative launch of the far read and the exchange (PeerExchange.read_merge); two launches
+        are faster on B200 (the fused kernel's tail costs its far-read loop a few per cent)."""
+        if self.exchange == "p2p" and fused:
+            n, hq, d = q.shape
+            if self.peer is None:
+                self.peer = PeerExchange(self.group, n=n, hq=hq, hd=d, device=q.device)
+            return self.peer.read_merge(self.ws, q, qsl, seq_lens, scale, out_l, lse_l, out)
+        o_all, lse_all = self.step(q, qsl, seq_lens, scale)
+        return self.merge(out_l, lse_l, o_all, lse_all, out, qsl, seq_lens)
 
     def merge(self, out_l, lse_l, o_all, lse_all, out, qsl, seq_lens):
         if self.exchange == "p2p":

@@ -252,6 +252,26 @@ int fold_exchange_merge(void* exchange, const float* o_part, const float* lse_pa
                         const int* qsl, const int* seq_lens, int n, int hq, int hd, int window, int block,
                         float inv_alpha, int* err, void* stream);
 
+/* The far read and the exchange in one kernel: on every rank, fold_far_read of this rank's chunk
+ * followed, in the same cooperative launch, by the work of fold_exchange_merge. Each CTA writes
+ * its split partial into o_part/lse_part (as fold_far_read; they stay scratch in L2) and counts it
+ * in the exchange's per-KV-head counter. Once every split of its KV head has finished (bounded
+ * wait), the head's CTAs share out the head's items: combine the splits, store the item into every
+ * peer over NVLink, wait for the peers' records and merge with the window read (o_l, lse_l) into
+ * `out`. This saves the separate exchange launch and its ramp. With an exchange of one rank it is
+ * the far read and the merge in one launch. Arguments as fold_far_read (without qf) and
+ * fold_exchange_merge; every rank passes the same `splits`, and splits * hkv CTAs must fit the
+ * device at once (one per SM). When the far read takes the tcgen05 kernel it issues fold_far_read
+ * and fold_exchange_merge as two launches. No reference counterpart (the reference runs on one
+ * GPU). */
+int fold_far_read_exchange(void* exchange, const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                           const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side,
+                           int pages, int64_t pos_lo, int64_t capacity, int* far_len, float* o_part, float* lse_part,
+                           int splits, const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head,
+                           const float* lse_l, int64_t ll_stride_head, int64_t ll_stride_tok, void* out,
+                           int64_t out_stride_tok, int64_t out_stride_head, int n, int hq, int hkv, int hd, int window,
+                           int block, int far_distance, float softmax_scale, float inv_alpha, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,3 +78,27 @@ def test_exchange_rejects_bad_arguments_without_a_gpu():
         _lib.call("fold_exchange_merge", None, None, None, 1, None, 0, 0, None, 0, 0, None, 0, 0, None, None, 1, 1,
                   128, 1, 1, 0.5, None, None)
     _lib.call("fold_exchange_destroy", None)  # destroying nothing is a no-op
+
+
+_CTYPES = {"void*": ctypes.c_void_p, "const void*": ctypes.c_void_p, "int*": ctypes.c_void_p,
+           "const int*": ctypes.c_void_p, "float*": ctypes.c_void_p, "const float*": ctypes.c_void_p,
+           "const int64_t*": ctypes.c_void_p, "void**": None, "int64_t": ctypes.c_int64, "int": ctypes.c_int,
+           "float": ctypes.c_float}
+
+
+def test_binding_argument_types_match_header():
+    """Every ctypes argument list has the header's arity and types, position by position."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, params in re.findall(r"\b(fold_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+        sig = _lib.SIGNATURES[name]
+        assert len(params) == len(sig), name
+        for p, t in zip(params, sig):
+            kind = re.sub(r"\s+", " ", p.rsplit(" ", 1)[0].replace(" *", "*")).strip()
+            if p.split()[-1].startswith("*"):
+                kind += "*"
+            want = _CTYPES[kind]
+            if want is None:  # void** out-parameter
+                assert t is not ctypes.c_int and t is not ctypes.c_float, (name, p)
+            else:
+                assert t is want, (name, p, t)

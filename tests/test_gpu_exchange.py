@@ -99,3 +99,60 @@ def test_exchange_rejects_a_larger_step_than_created_for():
             ex.merge(o, lse, o_l, lse_l, torch.empty_like(o_l), qsl, seq, window=2048, block=6, alpha=2.0)
     finally:
         ex.close()
+
+
+def far_case(seed, n, hq, hkv, hd, hist):
+    from fold_b200.attention import FoldWorkspace
+    from fold_b200.rope import default_inv_freq
+    from tests.helpers import side_from
+
+    rng = np.random.default_rng(seed)
+    W, B = 2048, n
+    seq = hist + n
+    k = rng.standard_normal((seq, hkv, hd), dtype=np.float32)
+    v = rng.standard_normal((seq, hkv, hd), dtype=np.float32)
+    q = torch.from_numpy(rng.standard_normal((n, hq, hd), dtype=np.float32)).cuda().to(torch.bfloat16)
+    dummy = torch.zeros((1, hkv, 16, 2 * hd), device="cuda", dtype=torch.bfloat16)
+    ws = FoldWorkspace(dummy, W, B, seq, inv_freq=default_inv_freq(500000.0, hd, "cuda"), far_distance=W + B,
+                       num_heads=hq)
+    ws.side = side_from(k, v, ws.side_pages)
+    o_l = torch.from_numpy(rng.standard_normal((n, hq, hd), dtype=np.float32)).cuda().to(torch.bfloat16)
+    lse_l = torch.from_numpy(rng.standard_normal((hq, n), dtype=np.float32) + 6).cuda()
+    qsl = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+    seq_t = torch.tensor([seq], dtype=torch.int32, device="cuda")
+    return ws, q, o_l, lse_l, qsl, seq_t
+
+
+@pytest.mark.parametrize("n,hq,hkv,hd,hist", [(10, 32, 8, 128, 40000), (8, 32, 8, 128, 2060), (3, 8, 2, 256, 9000),
+                                              (1, 4, 4, 128, 5000)])
+def test_single_rank_far_read_exchange_equals_far_read_and_merge(n, hq, hkv, hd, hist, far_kernel):
+    """fold_far_read_exchange with a one-rank exchange (far read + merge in one launch) against
+    fold_far_read followed by fold_merge: the same far partials, the same merge up to the order of
+    the split combine, so within one bf16 rounding."""
+    ws, q, o_l, lse_l, qsl, seq = far_case(hist + n, n, hq, hkv, hd, hist)
+    scale = hd ** -0.5
+    want = torch.empty((n, hq, hd), dtype=torch.bfloat16, device="cuda")
+    o_part, lse_part = ws.read_far(q, qsl, seq, scale)
+    kernels.merge(o_l, lse_l, o_part, lse_part, want, qsl, seq, window=ws.window, block=ws.block, alpha=ws.alpha)
+    ex = PeerExchange(n=n, hq=hq, hd=hd)
+    try:
+        got = torch.empty_like(want)
+        ex.read_merge(ws, q, qsl, seq, scale, o_l, lse_l, got)
+        torch.cuda.synchronize()
+        ws.check()
+        diff = (got.float() - want.float()).abs()
+        assert float(diff.max()) <= 2 ** -7 * float(want.float().abs().max())
+        # repeated launches and graph replays advance the epochs and reset the split counters
+        graph = torch.cuda.CUDAGraph()
+        outs = [torch.empty_like(want) for _ in range(3)]
+        with torch.cuda.graph(graph):
+            for o in outs:
+                ex.read_merge(ws, q, qsl, seq, scale, o_l, lse_l, o)
+        for _ in range(4):
+            graph.replay()
+        torch.cuda.synchronize()
+        ws.check()
+        assert all(torch.equal(o, got) for o in outs)
+        del graph
+    finally:
+        ex.close()

@@ -1,6 +1,8 @@
-"""The sharded far memory on 2 GPUs over NCCL with the CUDA kernels: each rank appends only its
-positions, reads its chunk, combines its splits and all-gathers; the merged output must match the
-unsharded far read + merge on one GPU. Skipped with fewer than 2 GPUs."""
+"""The sharded far memory on 2 and 4 GPUs with the CUDA kernels: each rank appends only its
+positions, reads its chunk, and the ranks' partials meet through NCCL (combine + all-gather +
+merge), the peer exchange kernel, or the far read that ends with the exchange (one cooperative
+launch); the merged output must match the unsharded far read + merge on one GPU. Skipped with
+fewer than 2 GPUs."""
 import datetime
 import os
 import socket
@@ -84,10 +86,11 @@ def worker(rank, world, port, q, exchange):
         ws = workspace(p, device, plan)
         sharded = ShardedFarMemory(plan, ws, exchange=exchange)
         out = step(p, ws, device, sharded)
-        replayed = None
+        replayed = fused = None
         if exchange == "p2p":
             replayed = replay(p, ws, device, sharded)
-        q.put((rank, "ok", (out.numpy(), replayed)))
+            fused = step_merge(p, ws, device, sharded)
+        q.put((rank, "ok", (out.numpy(), replayed, fused)))
     except Exception as e:
         q.put((rank, "error", repr(e)))
     finally:
@@ -95,6 +98,36 @@ def worker(rank, world, port, q, exchange):
             sharded.peer.close()
         if dist.is_initialized():
             dist.destroy_process_group()
+
+
+def step_merge(p, ws, device, sharded, steps=3, replays=4):
+    """The far read and the exchange in one cooperative launch (ShardedFarMemory.step_merge), eager
+    and in graph replays; returns the output (every replay must give it again, else None)."""
+    qsl = torch.tensor([0, p["n"]], dtype=torch.int32, device=device)
+    seq = torch.tensor([p["length"]], dtype=torch.int32, device=device)
+    outs = [torch.empty((p["n"], p["hq"], p["hd"]), device=device, dtype=torch.bfloat16) for _ in range(steps)]
+    scale = p["hd"] ** -0.5
+
+    def body():
+        for out in outs:
+            sharded.step_merge(p["q"], qsl, seq, scale, p["o_l"], p["lse_l"], out, fused=True)
+
+    body()
+    torch.cuda.synchronize(device)
+    first = outs[0].clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    same = all(torch.equal(o, first) for o in outs)
+    for _ in range(replays):
+        for o in outs:
+            o.zero_()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        same = same and all(torch.equal(o, first) for o in outs)
+    del graph
+    ws.check()
+    return first.float().cpu().numpy() if same else None
 
 
 def replay(p, ws, device, sharded, steps=4, replays=6):
@@ -147,10 +180,14 @@ def test_sharded_read_matches_single_gpu(world, exchange):
         pr.join(timeout=60)
     for r in range(world):
         assert res[r][0] == "ok", res[r]
-        out, replayed = res[r][1]
+        out, replayed, fused = res[r][1]
         assert np.abs(out - want).max() <= 2e-2
         if exchange == "p2p":
             assert replayed, "graph replays of the peer exchange changed the output"
+            # the far read and the exchange in one launch: same partials, same rank-order merge
+            assert fused is not None, "graph replays of the fused far read + exchange changed the output"
+            assert np.abs(fused - out).max() <= 2 ** -7 * np.abs(out).max()
+            assert np.array_equal(fused, res[0][1][2])
     # every rank holds the same merged output
     for r in range(1, world):
         assert np.array_equal(res[0][1][0], res[r][1][0])
