@@ -491,7 +491,7 @@ def run_gpu(args):
 def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err, append):
     """The window (exact-position) read, which the headline step takes as an input, measured on
     its own (16 splits per KV head) and inside the whole draft step: append + one launch of the far
-    read (splits - 1 per KV head) beside the window read (1 per KV head) + merge of both split
+    read (splits - 1 blocks per KV head) beside the window read (1 per KV head) + merge of both split
     sets. The drafter's paged cache (block size 16, shuffled blocks) holds every position a step's
     window reaches; each split reads a contiguous part of the window [H - W - B + 1, H + B)."""
     import numpy as np

@@ -135,7 +135,8 @@ class FoldWorkspace:
 
     def step_partials(self, n: int, num_heads: int):
         """(far, window) split buffers of the one-launch step read: splits() - 1 far splits beside
-        one window split per KV head, so that the launch stays one wave of CTAs."""
+        one window split per KV head, so that the launch is one wave of blocks (with one more far
+        split per head, the blocks beyond the device did not reliably start last)."""
         far = _partial_buffers(self._step_far, max(self.splits() - 1, 1), n, num_heads, self.head_dim, self.device)
         win = _partial_buffers(self._step_window, 1, n, num_heads, self.head_dim, self.device)
         return far, win

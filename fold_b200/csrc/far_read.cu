@@ -14,28 +14,33 @@ namespace fold {
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
-  split_read<C, false>(&map, nullptr, p, blockIdx.x);
+  split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y);
 }
 
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     window_read_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                        const FarParams p) {
-  split_read<C, true>(&kmap, &vmap, p, blockIdx.x);
+  split_read<C, true>(&kmap, &vmap, p, blockIdx.x, blockIdx.y);
 }
 
-// The far read and the window read of one draft step in one launch: per KV head, the first
-// win.splits CTAs read the window, the next far.splits the far memory. A window read is a few MB
-// and runs on its own SMs while the far read streams the side cache, so it adds no time to the
-// step when the grid fits the device in one wave.
+// The far read and the window read of one draft step in one launch, over a 1-D grid: blocks
+// [0, hkv * far.splits) read the far memory (KV head b / far.splits), the blocks after them read
+// the window. A window read is a few MB and runs on its own SMs while the far read streams the
+// side cache, which costs the step the window's bytes plus the far split it displaces when the
+// grid is one wave (one block per SM). A grid beyond the device is correct but slow: measured on
+// B200, some far blocks then started only when other far blocks finished.
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     step_read_kernel(const __grid_constant__ CUtensorMap far_map, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap, const FarParams far, const FarParams win) {
-  if (static_cast<int>(blockIdx.x) < win.splits)
-    split_read<C, true>(&kmap, &vmap, win, blockIdx.x);
-  else
-    split_read<C, false>(&far_map, nullptr, far, blockIdx.x - win.splits);
+  const int b = static_cast<int>(blockIdx.x), nfar = far.hkv * far.splits;
+  if (b < nfar) {
+    split_read<C, false>(&far_map, nullptr, far, b % far.splits, b / far.splits);
+  } else {
+    const int w = b - nfar;
+    split_read<C, true>(&kmap, &vmap, win, w % win.splits, w / win.splits);
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -203,8 +208,8 @@ struct StepLaunch {
     if (int s = side_tensor_map(side, pages, far.hkv, C::HD, C::TK, &map)) return s;
     static bool configured = false;  // per instantiation
     if (int e = allow_smem(step_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(step_read)")) return e;
-    step_read_kernel<C><<<dim3(win.splits + far.splits, far.hkv), C::NTHREADS, C::SMEM, stream>>>(map, kmap, vmap,
-                                                                                                   far, win);
+    const unsigned blocks = static_cast<unsigned>(far.hkv) * (far.splits + win.splits);
+    step_read_kernel<C><<<blocks, C::NTHREADS, C::SMEM, stream>>>(map, kmap, vmap, far, win);
     return check_launch("step_read_kernel");
   }
 };

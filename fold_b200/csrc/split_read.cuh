@@ -246,7 +246,7 @@ __device__ __forceinline__ void zero_v_rows(unsigned char* stage, int from) {
 //     query as given, row r reads its exact-position window (fold/attention.py:148-151,163).
 template <class C, bool WIN>
 __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
-                                           int split) {
+                                           int split, int h) {
   constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
   constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
   extern __shared__ unsigned char smem_raw[];
@@ -259,7 +259,6 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   float* row_inv = row_m + 64;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.y;
   const int G = p.group;
   const int nrows = p.n * G;
   const int RH = p.rot_dim >> 1;

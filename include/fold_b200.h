@@ -133,12 +133,12 @@ int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
  * fold_far_read (q_far, the rope table, the side cache, far_len, the far partials o_fpart/lse_fpart
  * with fsplits splits, far_scale = alpha * scale) and as fold_window_read (q_win, the paged cache,
  * its block table, the window, the window partials o_wpart/lse_wpart with wsplits splits,
- * win_scale = scale). Per KV head, wsplits CTAs read the window while fsplits CTAs read the far
- * memory, so the window read (a few MB) runs beside the far read instead of after it; choose
- * wsplits + fsplits <= SMs / hkv to keep one wave (e.g. wsplits = 1,
- * fsplits = fold_far_read_default_splits - 1). When the far read takes the tcgen05 kernel (see
- * fold_far_read_select_kernel) the two reads are issued as two launches. Merge the result with
- * fold_merge_partials. */
+ * win_scale = scale). The launch's blocks are hkv * fsplits far-read blocks followed by
+ * hkv * wsplits window-read blocks, so the window read (a few MB) runs beside the far read instead
+ * of after it. Keep hkv * (fsplits + wsplits) within one block per SM (e.g. wsplits = 1,
+ * fsplits = fold_far_read_default_splits - 1): blocks beyond the device may start only when far
+ * blocks finish. When the far read takes the tcgen05 kernel (see fold_far_read_select_kernel) the
+ * two reads are issued as two launches. Merge the result with fold_merge_partials. */
 int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_head, const void* q_win,
                    int64_t qw_stride_tok, int64_t qw_stride_head, const int* qsl, const int* seq_lens,
                    const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,

@@ -175,7 +175,8 @@ def test_step_read_equals_separate_reads(hd, hq, hkv, n, hist, far_kernel):
         return (torch.full((s, n, hq, hd), float("nan"), device="cuda"),
                 torch.full((s, hq, n), float("nan"), device="cuda"))
 
-    far_a, win_a, far_b, win_b = bufs(17), bufs(1), bufs(17), bufs(1)
+    fs = kernels.default_splits(hkv)  # one far block per SM: the window blocks overflow the device
+    far_a, win_a, far_b, win_b = bufs(fs), bufs(1), bufs(fs), bufs(1)
     kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, window=W, block=B, far_distance=W + B,
                       softmax_scale=scale, alpha=alpha, window_size=ws, causal=False, table=tab)
     kernels.far_read(qd, qsl, seq_t, side, far_b[0], far_b[1], window=W, block=B, far_distance=W + B,
