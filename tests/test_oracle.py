@@ -187,3 +187,35 @@ def test_combine_of_chunks_equals_single_read():
 def test_bf16_round_ties_to_even():
     x = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, 0.0], dtype=np.float32)
     np.testing.assert_array_equal(fo.bf16_round(x), [1.0, 1.0, 1.0 + 2 ** -6, -2.5, 0.0])
+
+
+def test_window_read_follows_flash_attention_window_rules():
+    """fo.window_read against a per-row loop over FlashAttention's bottom-right window rule
+    (key j < seq visible to row r at p = H + r iff p - left <= j <= p + right, and j <= p when
+    causal; a negative bound is unbounded), for the FOLD window, a native causal sliding window,
+    the unbounded causal case and a row with no key."""
+    rng = np.random.default_rng(3)
+    n, hq, hkv, d, hist = 4, 4, 2, 16, 37
+    seq = hist + n
+    q = rng.standard_normal((n, hq, d))
+    k = rng.standard_normal((seq, hkv, d))
+    v = rng.standard_normal((seq, hkv, d))
+    g = hq // hkv
+    for left, right, causal in [(9 + n - 1, n - 1, False), (5, 0, True), (-1, -1, True), (-1, 2, False)]:
+        o, lse = fo.window_read(q, k, v, hist, left, right, causal, 0.3)
+        for r in range(n):
+            p = hist + r
+            js = [j for j in range(seq) if (left < 0 or p - j <= left) and (right < 0 or j - p <= right)
+                  and (not causal or j <= p)]
+            for h in range(hq):
+                s = np.array([0.3 * q[r, h] @ k[j, h // g] for j in js])
+                m = s.max()
+                w = np.exp(s - m)
+                assert abs(lse[h, r] - (m + np.log(w.sum()))) < 1e-12
+                assert np.allclose(o[r, h], (w[:, None] * v[js, h // g]).sum(0) / w.sum(), atol=1e-12)
+    o1, l1 = fo.window_read(q, k, v, hist, 9 + n - 1, n - 1, False, 0.3)
+    o2, l2 = fo.local_read(q, k, v, hist, 9, n, 0.3)
+    assert np.array_equal(o1, o2) and np.array_equal(l1, l2)
+    # rows whose window holds no cached key are empty: o = 0, lse = -inf
+    o, lse = fo.window_read(q, k, v, hist, 0, 0, False, 0.3, keys_len=hist)
+    assert np.all(o == 0) and np.all(np.isneginf(lse))
