@@ -490,9 +490,10 @@ def run_gpu(args):
 
 def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err, append):
     """The window (exact-position) read, which the headline step takes as an input, measured on
-    its own (16 splits per KV head) and inside the whole draft step: append + one launch of the far
-    read (splits - 1 blocks per KV head) beside the window read (1 per KV head) + merge of both split
-    sets. The drafter's paged cache (block size 16, shuffled blocks) holds every position a step's
+    its own (16 splits per KV head) and inside the whole draft step: append + one launch in which
+    each KV head's blocks (one per SM in all) share the far and window reads, split per step from
+    the device-side lengths + merge of both split sets (with a tcgen05 far read, the two reads as
+    two launches, as FoldAttention does). The drafter's paged cache (block size 16, shuffled blocks) holds every position a step's
     window reaches; each split reads a contiguous part of the window [H - W - B + 1, H + B)."""
     import numpy as np
     import torch
@@ -512,9 +513,11 @@ def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_
     wo = torch.empty((wsplits, B, hq, hd), device=dev, dtype=torch.float32)
     wl = torch.empty((wsplits, hq, B), device=dev, dtype=torch.float32)
     scale = hd ** -0.5
-    fsplits = max(kernels.default_splits(hkv) - 1, 1)
+    fsplits = max(kernels.default_splits(hkv), 2)  # blocks per KV head, shared by the two reads
     far_parts = (torch.empty((fsplits, B, hq, hd), device=dev), torch.empty((fsplits, hq, B), device=dev))
-    win_parts = (torch.empty((1, B, hq, hd), device=dev), torch.empty((1, hq, B), device=dev))
+    win_parts = (torch.empty((fsplits, B, hq, hd), device=dev), torch.empty((fsplits, hq, B), device=dev))
+    plan = torch.zeros(1, device=dev, dtype=torch.int32)
+    one_launch = not kernels.far_read_uses_tcgen05(hd, B, hq, hkv)  # as FoldAttention chooses
     ws = (W + B - 1, B - 1)
 
     def window(i):
@@ -524,11 +527,18 @@ def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_
     def full_step(i):
         append(i)
         seq = seq_all[i: i + 1]
-        kernels.step_read(q_all[i], q_all[i], qsl, seq, side, far_parts, kc, vc, block_table, win_parts, window=W,
-                          block=B, far_distance=W + B, softmax_scale=scale, alpha=ALPHA, window_size=ws,
-                          causal=False, table=table, pos_lo=pos_lo, capacity=length, err=err)
-        kernels.merge_partials(win_parts[0], win_parts[1], far_parts[0], far_parts[1], out, qsl, seq, window=W,
-                               block=B, alpha=ALPHA)
+        if one_launch:
+            kernels.step_read(q_all[i], q_all[i], qsl, seq, side, far_parts, kc, vc, block_table, win_parts, plan,
+                              window=W, block=B, far_distance=W + B, softmax_scale=scale, alpha=ALPHA, window_size=ws,
+                              causal=False, table=table, pos_lo=pos_lo, capacity=length, err=err)
+            kernels.merge_partials(win_parts[0], win_parts[1], far_parts[0], far_parts[1], out, qsl, seq, window=W,
+                                   block=B, alpha=ALPHA, plan=plan)
+        else:  # tcgen05 far read, then the window read with its own splits
+            kernels.far_read(q_all[i], qsl, seq, side, far_parts[0], far_parts[1], window=W, block=B,
+                             far_distance=W + B, softmax_scale=scale * ALPHA, table=table, pos_lo=pos_lo,
+                             capacity=length, err=err)
+            window(i)
+            kernels.merge_partials(wo, wl, far_parts[0], far_parts[1], out, qsl, seq, window=W, block=B, alpha=ALPHA)
 
     def graph_of(fn):
         g = torch.cuda.CUDAGraph()
@@ -564,9 +574,10 @@ def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_
             "algorithmic_bytes": int(alg), "achieved_gbs": round(alg / (w_us * 1e-6) / 1e9, 1),
             "timing": "burst: K window reads back to back in one graph",
             "full_step_us": round(f_us, 3),
-            "full_step": f"append + one launch of the far read ({fsplits} splits per KV head) beside the window read "
-                         "(1 split per KV head) + merge of both split sets (no synthetic window input), one graph "
-                         "of K steps, sustained"}
+            "full_step": ("append + one launch in which the far and window reads share the KV heads' blocks "
+                          f"({fsplits} per head, split per step)" if one_launch else "append + tcgen05 far read + "
+                          f"window read ({wsplits} splits per KV head)") + " + merge of both split sets (no synthetic "
+                         "window input), one graph of K steps, sustained"}
 
 
 def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, rank, local, peer):

@@ -30,6 +30,7 @@ SIGNATURES = {
     "fold_far_read": [_vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp, _i64, _i64, _vp,
                       _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp],
     "fold_far_read_default_splits": [_i32, _i32, _i32, _i32],
+    "fold_far_read_kernel_for": [_i32, _i32, _i32, _i32],
     "fold_far_read_select_kernel": [_i32],
     "fold_merge": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp,
                    _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp],
@@ -37,10 +38,10 @@ SIGNATURES = {
     "fold_window_read": [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i64, _i64, _i64, _vp, _i32, _i32, _i32,
                          _i32, _f32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
     "fold_step_read": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp,
-                       _vp, _i32, _vp, _vp, _i64, _i32, _i64, _i64, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _i32,
+                       _vp, _vp, _vp, _i64, _i32, _i64, _i64, _i64, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _i32, _vp,
                        _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _vp, _vp],
-    "fold_merge_partials": [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
-                            _f32, _vp],
+    "fold_merge_partials": [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32,
+                            _i32, _f32, _vp],
     "fold_exchange_create": [_i32, _i32, _i64, _i32, ctypes.POINTER(ctypes.c_void_p), _vp],
     "fold_exchange_open": [_vp, _vp],
     "fold_exchange_destroy": [_vp],
@@ -100,3 +101,7 @@ def num_sms() -> int:
 
 def default_splits(hkv: int, hd: int, n: int, hq: int) -> int:
     return int(load().fold_far_read_default_splits(hkv, hd, n, hq))
+
+
+def far_read_kernel_for(hd: int, n: int, hq: int, hkv: int) -> int:
+    return int(load().fold_far_read_kernel_for(hd, n, hq, hkv))

@@ -90,14 +90,15 @@ class FoldWorkspace:
         self._parts = {}
         self._window_parts = {}
         self._step_far, self._step_window = {}, {}
+        self.plan = torch.zeros(1, device=cache.device, dtype=torch.int32)  # the step read's split
         if num_heads is not None:  # the buffers the forward of this layer uses, before any graph capture
-            if mode == "window" or self.sharded:
-                self.window_partials(self.block, int(num_heads))
-            if mode != "window":
-                if self.sharded:
-                    self.partials(self.block, int(num_heads))
-                else:
-                    self.step_partials(self.block, int(num_heads))
+            hq = int(num_heads)
+            if mode != "window" and self.one_launch(self.block, hq):
+                self.step_partials(self.block, hq)
+            else:
+                self.window_partials(self.block, hq)
+                if mode != "window":
+                    self.partials(self.block, hq)
 
     # -- derived state ---------------------------------------------------------------------------
     @property
@@ -133,12 +134,17 @@ class FoldWorkspace:
         """Split partial buffers of the window read (local_splits splits) for n rows."""
         return _partial_buffers(self._window_parts, self.local_splits, n, num_heads, self.head_dim, self.device)
 
+    def one_launch(self, n: int, num_heads: int) -> bool:
+        """Whether the far and window reads of a step of n rows run as one launch (read_step): for
+        an unsharded cache whose far read takes the mma.sync kernel."""
+        return not self.sharded and not kernels.far_read_uses_tcgen05(self.head_dim, n, num_heads, self.num_kv_heads)
+
     def step_partials(self, n: int, num_heads: int):
-        """(far, window) split buffers of the one-launch step read: splits() - 1 far splits beside
-        one window split per KV head, so that the launch is one wave of blocks (with one more far
-        split per head, the blocks beyond the device did not reliably start last)."""
-        far = _partial_buffers(self._step_far, max(self.splits() - 1, 1), n, num_heads, self.head_dim, self.device)
-        win = _partial_buffers(self._step_window, 1, n, num_heads, self.head_dim, self.device)
+        """(far, window) split buffers of the one-launch step read: splits() slots each (the
+        blocks of a KV head share the two reads, one block per SM in all)."""
+        s = max(self.splits(), 2)
+        far = _partial_buffers(self._step_far, s, n, num_heads, self.head_dim, self.device)
+        win = _partial_buffers(self._step_window, s, n, num_heads, self.head_dim, self.device)
         return far, win
 
     def check(self) -> None:
@@ -168,11 +174,12 @@ class FoldWorkspace:
                   rotate=True):
         """The far read of q (rotated, as read_far) and the window read of q_window over the
         drafter's paged cache kv_cache [blocks, Hkv, block_size, 2D] in one launch. Returns the
-        (far, window) split partials, for kernels.merge_partials."""
+        (far, window) split partials, for kernels.merge_partials with plan=self.plan."""
         n, hq, _ = q.shape
         far, win = self.step_partials(n, hq)
         k, v = kernels.paged_planes(kv_cache, self.head_dim)
-        kernels.step_read(q, q_window, qsl, seq_lens, self.side, far, k, v, block_table, win, window=self.window,
+        kernels.step_read(q, q_window, qsl, seq_lens, self.side, far, k, v, block_table, win, self.plan,
+                          window=self.window,
                           block=self.block, far_distance=self.far_distance, softmax_scale=scale, alpha=self.alpha,
                           window_size=window_size, causal=causal, table=self.table if rotate else None,
                           far_len=self.far_len, pos_lo=self.pos_lo, capacity=self.capacity, err=self.err)
@@ -223,21 +230,22 @@ class _Wrapped:
 
     def _fold_read(self, w, q_far, q_win, kv_cache, meta, out, *, window_size, causal, num_splits, rotate):
         """Far read + window read + merge of a FOLD layer into out [n, Hq, D]: one launch for both
-        reads when the window read is this package's and the side cache is not sharded."""
+        reads when the window read is this package's and the workspace allows it (one_launch)."""
         o, qsl, seq = self.original, meta.query_start_loc, meta.seq_lens
         local = dict(window_size=window_size, causal=causal, num_splits=num_splits, window=w.window,
                      block=w.block, alpha=w.alpha, err=w.err)
-        if self.local_read is None and not w.sharded:
+        n, hq = out.shape[0], out.shape[1]
+        if self.local_read is None and w.one_launch(n, hq):
             far, win = w.read_step(q_far, q_win, qsl, seq, o.scale, kv_cache, meta.block_table,
                                    window_size=window_size, causal=causal, rotate=rotate)
             kernels.merge_partials(win[0], win[1], far[0], far[1], out, qsl, seq, window=w.window, block=w.block,
-                                   alpha=w.alpha)
+                                   alpha=w.alpha, plan=w.plan)
             return
         if rotate:
             far = w.read_far(q_far, qsl, seq, o.scale)
         else:
             far = w.read_far(q_far, qsl, seq, o.scale, rotate=False)
-        parts = None if self.local_read is not None else w.window_partials(out.shape[0], out.shape[1])
+        parts = None if self.local_read is not None else w.window_partials(n, hq)
         self._window_and_merge(q_win, kv_cache, meta, parts, far, out, **local)
 
     def _window_and_merge(self, q, kv_cache, meta, parts, far, out, *, window_size, causal, num_splits, window,

@@ -111,64 +111,6 @@ int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int b
   return FOLD_OK;
 }
 
-namespace {
-struct PagedKey {
-  uintptr_t ptr;
-  int64_t num_blocks, s_block, s_slot, s_head;
-  int block_size, hkv, hd, device;
-  bool operator==(const PagedKey& o) const {
-    return ptr == o.ptr && num_blocks == o.num_blocks && s_block == o.s_block && s_slot == o.s_slot &&
-           s_head == o.s_head && block_size == o.block_size && hkv == o.hkv && hd == o.hd && device == o.device;
-  }
-};
-struct PagedKeyHash {
-  size_t operator()(const PagedKey& k) const {
-    size_t h = std::hash<uintptr_t>()(k.ptr);
-    for (int64_t v : {k.num_blocks, k.s_block, k.s_slot, k.s_head, static_cast<int64_t>(k.block_size),
-                      static_cast<int64_t>(k.hkv) << 20 | k.hd, static_cast<int64_t>(k.device)})
-      h ^= std::hash<int64_t>()(v) + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
-    return h;
-  }
-};
-std::unordered_map<PagedKey, CUtensorMap, PagedKeyHash> g_paged_maps;
-}  // namespace
-
-int paged_tensor_map(const void* base, int64_t num_blocks, int block_size, int hkv, int hd, int64_t s_block,
-                     int64_t s_slot, int64_t s_head, CUtensorMap* out) {
-  int dev = 0;
-  if (int s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return s;
-  PagedKey key{reinterpret_cast<uintptr_t>(base), num_blocks, s_block, s_slot, s_head, block_size, hkv, hd, dev};
-  std::lock_guard<std::mutex> lock(g_map_mutex);
-  auto it = g_paged_maps.find(key);
-  if (it != g_paged_maps.end()) {
-    *out = it->second;
-    return FOLD_OK;
-  }
-  if (int s = load_encode()) return s;
-  if (!aligned16(base)) return fail(FOLD_ERR_ALIGNMENT, "paged cache pointer is not 16-byte aligned");
-  // Dimensions in increasing stride order: (hd, slot, head, block), or (hd, head, slot, block) when
-  // the heads of a slot are adjacent; the box is 16 slots of one head either way.
-  const bool head_inner = s_head < s_slot;
-  const cuuint64_t d_slot = static_cast<cuuint64_t>(block_size), d_head = static_cast<cuuint64_t>(hkv);
-  const cuuint64_t st_slot = static_cast<cuuint64_t>(s_slot) * 2u, st_head = static_cast<cuuint64_t>(s_head) * 2u;
-  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(hd), head_inner ? d_head : d_slot, head_inner ? d_slot : d_head,
-                              static_cast<cuuint64_t>(num_blocks)};
-  const cuuint64_t strides[3] = {head_inner ? st_head : st_slot, head_inner ? st_slot : st_head,
-                                 static_cast<cuuint64_t>(s_block) * 2u};
-  const cuuint32_t box[4] = {64u, head_inner ? 1u : 16u, head_inner ? 16u : 1u, 1u};
-  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  CUtensorMap m;
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(FOLD_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled (paged cache) failed with CUresult " + std::to_string(r));
-  if (g_paged_maps.size() > 4096) g_paged_maps.clear();
-  g_paged_maps.emplace(key, m);
-  *out = m;
-  return FOLD_OK;
-}
-
 }  // namespace fold
 
 extern "C" {

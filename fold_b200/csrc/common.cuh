@@ -1,5 +1,5 @@
 // Shared device helpers for the FOLD sm_100a kernels: mbarriers with bounded waits, TMA tile
-// loads, ldmatrix/movmatrix, bf16 mma.sync, named barriers, fast exp2.
+// loads, cp.async, ldmatrix, bf16 mma.sync, named barriers, fast exp2.
 #pragma once
 
 #include <cuda.h>
@@ -80,20 +80,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
       : "memory");
 }
-// 4-D tiled load global -> shared (the paged-cache read: column, slot, head, block).
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
-                                            int c2, int c3, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
-      : "memory");
+// 16-byte asynchronous copy global -> shared through L2 (cp.async.cg); the bytes past src_bytes
+// (all 16 when src_bytes is 0) are zero-filled, and src is not read beyond src_bytes.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
-// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA)
-// accesses of the same memory.
-__device__ __forceinline__ void fence_proxy_async_shared() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// Arrives on `bar` once every earlier cp.async of this thread has completed (the arrival is one of
+// the barrier's expected count: no increment).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

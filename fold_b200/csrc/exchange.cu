@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) exchange_merge_kernel(const 
     const int t = th / m.hq, h = th - (th / m.hq) * m.hq;
     const int col = slice * kSlice + lane * 4;
     float of[4], lse_far;
-    combine_slice(m, t, h, col, active, true, sums, of, lse_far);
+    combine_slice(m, t, h, col, active, true, sums, of, lse_far, m.splits);
     epoch = s_epoch;
     if (warp == 0) {
       // window read first: its loads overlap the pushes and the wait

@@ -132,7 +132,7 @@ template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     far_exchange_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ FarParams p,
                         const __grid_constant__ TailParams t) {
-  split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y);
+  split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
   exchange_tail<C::NW>(p, t, blockIdx.x, blockIdx.y);
 }
 

@@ -19,14 +19,13 @@ int make_far_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, 
                     float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd, int window, int block,
                     int far_distance, float softmax_scale, int* err, FarParams* out);
 
-// Checks the arguments of a window read (those of fold_window_read), fills its parameter block and
-// the TMA descriptors of the K and V planes.
+// Checks the arguments of a window read (those of fold_window_read) and fills its parameter block.
 int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,
                        const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
                        int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
                        const int* block_table, int block_table_len, int window_left, int window_right, int causal,
                        float softmax_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
-                       int* err, FarParams* out, CUtensorMap* kmap, CUtensorMap* vmap);
+                       int* err, FarParams* out);
 
 // Calls f.run<FarCfg<HD, nt, TK, HG>>() for nt in 1..8 (n * G query rows in n8 tiles).
 template <int HD, int TK, int HG, class F>

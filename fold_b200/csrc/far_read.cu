@@ -14,33 +14,54 @@ namespace fold {
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
-  split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y);
+  split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::NTHREADS, 1)
-    window_read_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                       const FarParams p) {
-  split_read<C, true>(&kmap, &vmap, p, blockIdx.x, blockIdx.y);
+__global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarParams p) {
+  split_read<C, true>(nullptr, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
-// The far read and the window read of one draft step in one launch, over a 1-D grid: blocks
-// [0, hkv * far.splits) read the far memory (KV head b / far.splits), the blocks after them read
-// the window. A window read is a few MB and runs on its own SMs while the far read streams the
-// side cache, which costs the step the window's bytes plus the far split it displaces when the
-// grid is one wave (one block per SM). A grid beyond the device is correct but slow: measured on
-// B200, some far blocks then started only when other far blocks finished.
+// A window tile costs about this many far tiles (in tenths): the window read copies 16-byte chunks
+// with cp.async, which one SM issues at about half the rate TMA moves the far read's boxes.
+constexpr int kWindowTileCost10 = 23;
+
+// How many of a KV head's S blocks read the window in this step (the rest read the far memory),
+// from the device-side lengths: the count in [1, S - 1] whose slower side finishes first. Every
+// block of the launch computes the same count.
 template <class C>
-__global__ void __launch_bounds__(C::NTHREADS, 1)
-    step_read_kernel(const __grid_constant__ CUtensorMap far_map, const __grid_constant__ CUtensorMap kmap,
-                     const __grid_constant__ CUtensorMap vmap, const FarParams far, const FarParams win) {
-  const int b = static_cast<int>(blockIdx.x), nfar = far.hkv * far.splits;
-  if (b < nfar) {
-    split_read<C, false>(&far_map, nullptr, far, b % far.splits, b / far.splits);
-  } else {
-    const int w = b - nfar;
-    split_read<C, true>(&kmap, &vmap, win, w % win.splits, w / win.splits);
+__device__ __forceinline__ int window_blocks(const FarParams& far, const FarParams& win, int S) {
+  const int qlen = far.qsl[1] - far.qsl[0];
+  const int seq = far.seq[0];
+  const int hist = max(seq - qlen, 0);
+  int64_t pos0, end;
+  const int F = far_tiles<C::TK>(far, hist, &pos0, &end);
+  const int Wt = window_tiles<C::TK>(win, hist, seq, &pos0, &end);
+  int best = 1, best_t = 0x7fffffff;
+  for (int w = 1; w < S; ++w) {
+    const int tf = 10 * ((F + (S - w) - 1) / (S - w));
+    const int tw = kWindowTileCost10 * ((Wt + w - 1) / w);
+    const int t = tf > tw ? tf : tw;
+    if (t < best_t) best_t = t, best = w;
   }
+  return best;
+}
+
+// The far read and the window read of one draft step in one launch: of the S = gridDim.x blocks
+// of KV head blockIdx.y, the first w (window_blocks) read the window into window slots [0, w) and
+// the others the far memory into far slots [0, S - w), so the window read (a few MB) runs beside
+// the far read instead of after it. Block (0, 0) stores w in plan[0] for the merge.
+template <class C>
+__global__ void __launch_bounds__(C::NTHREADS, 1)
+    step_read_kernel(const __grid_constant__ CUtensorMap far_map, const FarParams far, const FarParams win,
+                     int* plan) {
+  const int S = static_cast<int>(gridDim.x), x = static_cast<int>(blockIdx.x), h = static_cast<int>(blockIdx.y);
+  const int w = window_blocks<C>(far, win, S);
+  if (x == 0 && h == 0 && threadIdx.x == 0) *plan = w;
+  if (x < w)
+    split_read<C, true>(nullptr, nullptr, win, x, h, w);
+  else
+    split_read<C, false>(&far_map, nullptr, far, x - w, h, S - w);
 }
 
 // ------------------------------------------------------------------ host side
@@ -116,15 +137,13 @@ int make_far_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, 
   return FOLD_OK;
 }
 
-// Checks the arguments of a window read (those of fold_window_read), fills its parameter block and
-// the TMA descriptors of the K and V planes.
-int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
-                              const int* seq_lens, const void* k_cache, const void* v_cache, int64_t num_blocks,
-                              int block_size, int64_t cache_stride_block, int64_t cache_stride_head,
-                              int64_t cache_stride_slot, const int* block_table, int block_table_len,
-                              int window_left, int window_right, int causal, float softmax_scale, float* o_part,
-                              float* lse_part, int splits, int n, int hq, int hkv, int hd, int* err, FarParams* out,
-                              CUtensorMap* kmap, CUtensorMap* vmap) {
+// Checks the arguments of a window read (those of fold_window_read) and fills its parameter block.
+int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,
+                       const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
+                       int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
+                       const int* block_table, int block_table_len, int window_left, int window_right, int causal,
+                       float softmax_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
+                       int* err, FarParams* out) {
   if (!q || !qsl || !seq_lens || !k_cache || !v_cache || !block_table || !o_part || !lse_part)
     return fail(FOLD_ERR_INVALID_ARGUMENT, "window read: null pointer");
   if (n < 1 || hq < 1 || hkv < 1 || hq % hkv || splits < 1 || splits > 65535 || block_table_len < 1)
@@ -138,12 +157,6 @@ int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
       cache_stride_head % 8 || cache_stride_slot % 8 || !aligned16(k_cache) || !aligned16(v_cache))
     return fail(FOLD_ERR_ALIGNMENT, "window read: cache planes must be 16-byte aligned with strides of 8 elements");
   if (n * (hq / hkv) > 64) return fail(FOLD_ERR_UNSUPPORTED, "window read: n * (hq / hkv) must be at most 64");
-  if (int s = paged_tensor_map(k_cache, num_blocks, block_size, hkv, hd, cache_stride_block, cache_stride_slot,
-                               cache_stride_head, kmap))
-    return s;
-  if (int s = paged_tensor_map(v_cache, num_blocks, block_size, hkv, hd, cache_stride_block, cache_stride_slot,
-                               cache_stride_head, vmap))
-    return s;
   FarParams prm{};
   prm.q = static_cast<const __nv_bfloat16*>(q);
   prm.q_st = q_stride_tok, prm.q_sh = q_stride_head;
@@ -153,10 +166,11 @@ int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
   prm.scale_log2 = softmax_scale * kLog2e;
   prm.err = err;
   prm.vec_rot = vec_rotation_ok(q, q_stride_tok, q_stride_head, nullptr, 0, 0, nullptr, 0, hd);
+  prm.kc = static_cast<const __nv_bfloat16*>(k_cache), prm.vc = static_cast<const __nv_bfloat16*>(v_cache);
+  prm.s_block = cache_stride_block, prm.s_head = cache_stride_head, prm.s_slot = cache_stride_slot;
   prm.block_table = block_table, prm.bt_len = block_table_len;
   prm.num_blocks = static_cast<int>(num_blocks), prm.block_size = block_size;
   prm.win_left = window_left, prm.win_right = window_right, prm.causal = causal ? 1 : 0;
-  prm.head_inner = cache_stride_head < cache_stride_slot ? 1 : 0;  // as paged_tensor_map orders the dims
   *out = prm;
   return FOLD_OK;
 }
@@ -182,14 +196,12 @@ struct FarLaunch {
 
 struct WindowLaunch {
   const FarParams& prm;
-  const CUtensorMap& kmap;
-  const CUtensorMap& vmap;
   cudaStream_t stream;
   template <class C>
   int run() const {
     static bool configured = false;  // per instantiation
     if (int e = allow_smem(window_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(window_read)")) return e;
-    window_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(kmap, vmap, prm);
+    window_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(prm);
     return check_launch("window_read_kernel");
   }
 };
@@ -199,8 +211,7 @@ struct StepLaunch {
   const FarParams& win;
   const void* side;
   int pages;
-  const CUtensorMap& kmap;
-  const CUtensorMap& vmap;
+  int* plan;
   cudaStream_t stream;
   template <class C>
   int run() const {
@@ -208,8 +219,7 @@ struct StepLaunch {
     if (int s = side_tensor_map(side, pages, far.hkv, C::HD, C::TK, &map)) return s;
     static bool configured = false;  // per instantiation
     if (int e = allow_smem(step_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(step_read)")) return e;
-    const unsigned blocks = static_cast<unsigned>(far.hkv) * (far.splits + win.splits);
-    step_read_kernel<C><<<blocks, C::NTHREADS, C::SMEM, stream>>>(map, kmap, vmap, far, win);
+    step_read_kernel<C><<<dim3(far.splits, far.hkv), C::NTHREADS, C::SMEM, stream>>>(map, far, win, plan);
     return check_launch("step_read_kernel");
   }
 };
@@ -238,6 +248,11 @@ int fold_far_read_select_kernel(int kernel) {
   if (kernel < -1 || kernel > 1) return fold::fail(FOLD_ERR_INVALID_ARGUMENT, "far read kernel: -1, 0 or 1");
   fold::g_far_variant.store(kernel);
   return FOLD_OK;
+}
+
+int fold_far_read_kernel_for(int hd, int n, int hq, int hkv) {
+  if (hd < 1 || n < 1 || hq < 1 || hkv < 1 || hq % hkv) return -1;
+  return fold::far_read_variant(hd, n * (hq / hkv));
 }
 
 int fold_far_read_default_splits(int hkv, int hd, int n, int hq) {
@@ -273,44 +288,42 @@ int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                      int* err, void* stream) {
   using namespace fold;
   FarParams prm;
-  CUtensorMap kmap, vmap;
   if (int s = make_window_params(q, q_stride_tok, q_stride_head, qsl, seq_lens, k_cache, v_cache, num_blocks,
                                  block_size, cache_stride_block, cache_stride_head, cache_stride_slot, block_table,
                                  block_table_len, window_left, window_right, causal, softmax_scale, o_part, lse_part,
-                                 splits, n, hq, hkv, hd, err, &prm, &kmap, &vmap))
+                                 splits, n, hq, hkv, hd, err, &prm))
     return s;
-  return with_mma_config(hd, n * (hq / hkv), WindowLaunch{prm, kmap, vmap, static_cast<cudaStream_t>(stream)});
+  return with_mma_config(hd, n * (hq / hkv), WindowLaunch{prm, static_cast<cudaStream_t>(stream)});
 }
 
 int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_head, const void* q_win,
                    int64_t qw_stride_tok, int64_t qw_stride_head, const int* qsl, const int* seq_lens,
                    const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
-                   int64_t capacity, int* far_len, float* o_fpart, float* lse_fpart, int fsplits,
-                   const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
-                   int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
-                   const int* block_table, int block_table_len, int window_left, int window_right, int causal,
-                   float* o_wpart, float* lse_wpart, int wsplits, int n, int hq, int hkv, int hd, int window,
-                   int block, int far_distance, float far_scale, float win_scale, int* err, void* stream) {
+                   int64_t capacity, int* far_len, float* o_fpart, float* lse_fpart, const void* k_cache,
+                   const void* v_cache, int64_t num_blocks, int block_size, int64_t cache_stride_block,
+                   int64_t cache_stride_head, int64_t cache_stride_slot, const int* block_table, int block_table_len,
+                   int window_left, int window_right, int causal, float* o_wpart, float* lse_wpart, int splits,
+                   int* plan, int n, int hq, int hkv, int hd, int window, int block, int far_distance, float far_scale,
+                   float win_scale, int* err, void* stream) {
   using namespace fold;
+  if (!plan) return fail(FOLD_ERR_INVALID_ARGUMENT, "step read: null plan");
   FarParams far, win;
-  CUtensorMap kmap, vmap;
   if (int s = make_far_params(q_far, qf_stride_tok, qf_stride_head, qsl, seq_lens, rope_table, table_rows, rot_dim,
-                              side, pages, pos_lo, capacity, far_len, nullptr, 0, 0, o_fpart, lse_fpart, fsplits, n,
+                              side, pages, pos_lo, capacity, far_len, nullptr, 0, 0, o_fpart, lse_fpart, splits, n,
                               hq, hkv, hd, window, block, far_distance, far_scale, err, &far))
     return s;
   if (int s = make_window_params(q_win, qw_stride_tok, qw_stride_head, qsl, seq_lens, k_cache, v_cache, num_blocks,
                                  block_size, cache_stride_block, cache_stride_head, cache_stride_slot, block_table,
                                  block_table_len, window_left, window_right, causal, win_scale, o_wpart, lse_wpart,
-                                 wsplits, n, hq, hkv, hd, err, &win, &kmap, &vmap))
+                                 splits, n, hq, hkv, hd, err, &win))
     return s;
-  if (fsplits + wsplits > 65535) return fail(FOLD_ERR_INVALID_ARGUMENT, "step read: too many splits");
   const int rows = n * (hq / hkv);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (far_read_variant(hd, rows) == 1) {  // the tcgen05 far read has no window mode: two launches
-    if (int s = far_read_tc_launch(far, side, pages, hd, ((rows + 15) / 16) * 16, true, st)) return s;
-    return with_mma_config(hd, rows, WindowLaunch{win, kmap, vmap, st});
-  }
-  return with_mma_config(hd, rows, StepLaunch{far, win, side, pages, kmap, vmap, st});
+  if (far_read_variant(hd, rows) == 1)
+    return fail(FOLD_ERR_UNSUPPORTED,
+                "step read: this shape's far read takes the tcgen05 kernel (fold_far_read_kernel_for); issue "
+                "fold_far_read and fold_window_read");
+  if (splits < 2) return fail(FOLD_ERR_INVALID_ARGUMENT, "step read: at least 2 blocks per KV head");
+  return with_mma_config(hd, rows, StepLaunch{far, win, side, pages, plan, static_cast<cudaStream_t>(stream)});
 }
 
 }  // extern "C"

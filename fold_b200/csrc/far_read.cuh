@@ -29,11 +29,14 @@ struct FarParams {
   float scale_log2;
   int* err;
   int vec_rot;  // q, qf and the table rows allow the 16-byte vector path of the rotation
-  // Window read only (window_read_kernel): the paged cache, its block table and the window.
+  // Window read only (window_read_kernel): the paged cache's K and V planes (strides in elements),
+  // its block table and the window.
+  const __nv_bfloat16* kc;
+  const __nv_bfloat16* vc;
+  int64_t s_block, s_head, s_slot;
   const int* block_table;
   int bt_len, num_blocks, block_size;
   int win_left, win_right, causal;
-  int head_inner;  // the paged map's coordinates are (col, head, slot, block) instead of (col, slot, head, block)
 };
 
 constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100

@@ -29,13 +29,6 @@ int side_tensor_map(const void* side, int pages, int hkv, int hd, int box_rows, 
 // The same descriptor, encoded into *out on every call without touching the cache (no heap use).
 int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out);
 
-// 4-D TMA descriptor of one plane (K or V) of a paged cache, bf16, innermost dim contiguous,
-// strides in elements (multiples of 8), 128-byte swizzle, box of 64 columns x 16 slots of one
-// head. Its dimensions are (hd, slot, head, block), or (hd, head, slot, block) when
-// s_head < s_slot (coordinates in that order). Cached per (pointer, shape, strides).
-int paged_tensor_map(const void* base, int64_t num_blocks, int block_size, int hkv, int hd, int64_t s_block,
-                     int64_t s_slot, int64_t s_head, CUtensorMap* out);
-
 int device_sm_count();
 
 // Far read into caller-given partial buffers with the descriptor built on the stack; the

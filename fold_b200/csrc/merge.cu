@@ -22,7 +22,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
   const int col = slice * kSlice + lane * 4;
   const bool has_far = FINAL ? row_has_far(p, t) : true;
   float of[4], lse_far;
-  combine_slice(p, t, h, col, active, has_far, sums, of, lse_far);
+  combine_slice(p, t, h, col, active, has_far, sums, of, lse_far, p.splits);
   if (warp != 0) return;
   if constexpr (FINAL) {
     if (active) merge_store(p, t, h, col, of, lse_far);
@@ -37,21 +37,25 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
 
 // Both sides as split partials: the window read's splits (pw) are combined by log-sum-exp, then
 // the far read's (pf, which also carries the output and the step geometry), and the two are merged
-// with the alpha weighting. Without far splits the output is the combined window read.
+// with the alpha weighting. Without far splits the output is the combined window read. With
+// `plan` (the step read's device word), the window set uses its first plan[0] slots and the far
+// set its first pw.splits - plan[0].
 __global__ void __launch_bounds__(kMergeWarps * 32)
-    merge_partials_kernel(const MergeParams pw, const MergeParams pf, int slices, int hd) {
+    merge_partials_kernel(const MergeParams pw, const MergeParams pf, const int* plan, int slices, int hd) {
   __shared__ SliceSums sums;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slice = blockIdx.x % slices, th = blockIdx.x / slices;
   const int t = th / pf.hq, h = th - (th / pf.hq) * pf.hq;
   const bool active = lane * 4 < min(hd, kSlice);
   const int col = slice * kSlice + lane * 4;
+  const int wsplits = plan ? min(max(*plan, 0), pw.splits) : pw.splits;
+  const int fsplits = plan ? pw.splits - wsplits : pf.splits;
   float ol[4], ll;
-  combine_slice(pw, t, h, col, active, true, sums, ol, ll);
+  combine_slice(pw, t, h, col, active, true, sums, ol, ll, wsplits);
   float of[4] = {0.f, 0.f, 0.f, 0.f}, lf = -INFINITY;
   if (pf.splits > 0) {
     __syncthreads();  // warp 0 has read the window sums
-    combine_slice(pf, t, h, col, active, row_has_far(pf, t), sums, of, lf);
+    combine_slice(pf, t, h, col, active, row_has_far(pf, t), sums, of, lf, fsplits);
   }
   if (warp != 0 || !active) return;
   merge_store_loaded(pf, t, h, col, of, lf, ol, ll);
@@ -126,13 +130,15 @@ int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, c
 }
 
 int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplits, const float* o_fpart,
-                        const float* lse_fpart, int fsplits, void* out, int64_t out_stride_tok,
+                        const float* lse_fpart, int fsplits, const int* plan, void* out, int64_t out_stride_tok,
                         int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd,
                         int window, int block, float inv_alpha, void* stream) {
   using namespace fold;
   if (!o_wpart || !lse_wpart || !out || !qsl || !seq_lens || (fsplits > 0 && (!o_fpart || !lse_fpart)))
     return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: null pointer");
   if (n < 1 || hq < 1 || wsplits < 1 || fsplits < 0) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: bad sizes");
+  if (plan && fsplits != wsplits)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: with a step plan both sets have the same slot count");
   if (hd < 8 || (hd > kSlice && hd % kSlice) || (hd <= kSlice && hd % 4))
     return fail(FOLD_ERR_UNSUPPORTED, "merge partials: head size must be a multiple of 128, or of 4 up to 128");
   if (out_stride_tok % 2 || out_stride_head % 2 || (reinterpret_cast<uintptr_t>(out) & 3) ||
@@ -153,7 +159,7 @@ int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplit
   const int64_t blocks = static_cast<int64_t>(n) * hq * slices;
   if (blocks > 2147483647) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: too many rows");
   merge_partials_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      pw, pf, slices, hd);
+      pw, pf, plan, slices, hd);
   return check_launch("merge_partials_kernel");
 }
 

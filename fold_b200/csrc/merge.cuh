@@ -75,28 +75,29 @@ struct SliceSums {
   float w[kMergeWarps];
 };
 
-// Log-sum-exp combine of the far partials of (row t, head h) on the columns [col, col + 4) of
-// each lane, by all kMergeWarps warps of the block: every warp takes a share of the splits, loads
+// Log-sum-exp combine of the first `splits` far partials of (row t, head h) on the columns
+// [col, col + 4) of each lane, by all kMergeWarps warps of the block: every warp takes a share of the splits, loads
 // its partial rows in batches of independent loads (they sit in L2 after the far read), and the
 // weighted sums meet in shared memory. Warp 0 returns the normalised combined values `of` and the
 // combined LSE (-inf when no split holds a key); the other warps' outputs are meaningless. Ends
 // with the block barrier after which warp 0 has read the shared sums: the caller needs another
 // barrier before `sums` is written again.
 __device__ __forceinline__ void combine_slice(const MergeParams& p, int t, int h, int col, bool active,
-                                              bool has_far, SliceSums& sums, float (&of)[4], float& lse_far) {
+                                              bool has_far, SliceSums& sums, float (&of)[4], float& lse_far,
+                                              int splits) {
   constexpr int BATCH = 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* lf = p.lse_f + static_cast<int64_t>(h) * p.lf_sh + static_cast<int64_t>(t) * p.lf_st;
   float mx = -INFINITY;
   if (has_far) {
-    for (int s = lane; s < p.splits; s += 32) mx = fmaxf(mx, lf[s * p.lf_ss]);
+    for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, lf[s * p.lf_ss]);
     mx = warp_max(mx);
   }
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float wsum = 0.f;
   if (mx != -INFINITY) {
-    const int per = (p.splits + kMergeWarps - 1) / kMergeWarps;
-    const int s0 = warp * per, s1 = min(p.splits, s0 + per);
+    const int per = (splits + kMergeWarps - 1) / kMergeWarps;
+    const int s0 = warp * per, s1 = min(splits, s0 + per);
     const int64_t base = static_cast<int64_t>(t) * p.of_st + static_cast<int64_t>(h) * p.of_sh + col;
     for (int sb = s0; sb < s1; sb += 32) {
       const int cnt = min(32, s1 - sb);
@@ -104,10 +105,11 @@ __device__ __forceinline__ void combine_slice(const MergeParams& p, int t, int h
       const float w = l == -INFINITY ? 0.f : expf(l - mx);  // an empty split carries no mass
       wsum += w;
       for (int j = 0; j < cnt; j += BATCH) {
-        float v[BATCH][4];
+        float v[BATCH][4], wu[BATCH];
 #pragma unroll
         for (int u = 0; u < BATCH; ++u) {
-          if (active && j + u < cnt) {
+          wu[u] = __shfl_sync(0xffffffffu, w, (j + u) & 31);
+          if (active && j + u < cnt && wu[u] > 0.f) {  // an empty split's o is not read
             load_row<4>(p.o_f, p.of_bf16, base + (sb + j + u) * p.of_ss, v[u]);
           } else {
             v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
@@ -115,10 +117,9 @@ __device__ __forceinline__ void combine_slice(const MergeParams& p, int t, int h
         }
 #pragma unroll
         for (int u = 0; u < BATCH; ++u) {
-          const float wu = __shfl_sync(0xffffffffu, w, (j + u) & 31);
-          if (j + u < cnt) {
+          if (j + u < cnt && wu[u] > 0.f) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = fmaf(wu, v[u][i], acc[i]);
+            for (int i = 0; i < 4; ++i) acc[i] = fmaf(wu[u], v[u][i], acc[i]);
           }
         }
       }

@@ -79,42 +79,59 @@ __device__ __forceinline__ void issue_tile(unsigned char* smem, uint64_t* full, 
   for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
 }
 
-// Window read: issues the copies of the tile of positions [tpos, tpos + TK) of head h from the
-// paged cache into stage `st`, in 16-position chunks (every block size is a multiple of 16, so a
-// chunk never straddles two blocks). Each chunk lands where a TK-row box would have put it, so
-// the stage has the far read's layout. Chunks past the last context entry reload the last valid
-// chunk (the consumers zero those V rows and mask those keys); a block-table entry outside the
-// cache records FOLD_DEVERR_BLOCK_TABLE and reads block 0 instead.
+// Window read: the cache block that holds a warp's rows of the tile at tpos (the warp's TK / 8
+// rows lie in one 16-position chunk of one block: every block size is a multiple of 16), or -1
+// past the context. An entry outside the cache records FOLD_DEVERR_BLOCK_TABLE and reads as -1.
 template <class C>
-__device__ __forceinline__ void issue_window_tile(unsigned char* smem, uint64_t* full, const CUtensorMap* kmap,
-                                                  const CUtensorMap* vmap, int st, int64_t tpos, int seq, int h,
-                                                  const FarParams& p, uint64_t pol) {
-  constexpr int CH = C::TK / 16;
-  const int64_t last = (static_cast<int64_t>(seq - 1) / 16) * 16;  // a tile exists only when seq >= 1
-  int blk[CH], slot[CH];
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {  // all table loads first: one latency for the whole tile
-    const int64_t pos = min64(tpos + 16 * c, last);
-    const int lb = static_cast<int>(pos / p.block_size);
-    slot[c] = static_cast<int>(pos - static_cast<int64_t>(lb) * p.block_size);
-    blk[c] = lb < p.bt_len ? __ldg(p.block_table + lb) : -1;
+__device__ __forceinline__ int window_block(const FarParams& p, int64_t tpos, int seq) {
+  const int64_t pos = tpos + (threadIdx.x >> 5) * (C::TK / C::NW);
+  if (pos >= seq) return -1;
+  const int64_t lb = pos / p.block_size;
+  const int blk = lb < p.bt_len ? __ldg(p.block_table + lb) : -1;
+  if (blk < 0 || blk >= p.num_blocks) {
+    set_error(p.err, FOLD_DEVERR_BLOCK_TABLE);
+    return -1;
   }
-  mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
-  unsigned char* dst = smem + st * C::STAGE_BYTES;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    int b = blk[c];
-    if (b < 0 || b >= p.num_blocks) {
-      set_error(p.err, FOLD_DEVERR_BLOCK_TABLE);
-      b = 0;
-    }
-    const int c1 = p.head_inner ? h : slot[c], c2 = p.head_inner ? slot[c] : h;
-#pragma unroll
-    for (int x = 0; x < C::KBOX; ++x) {
-      tma_load_4d(dst + x * C::BOX_BYTES + c * 2048, kmap, &full[st], x * 64, c1, c2, b, pol);
-      tma_load_4d(dst + (C::KBOX + x) * C::BOX_BYTES + c * 2048, vmap, &full[st], x * 64, c1, c2, b, pol);
-    }
+  return blk;
+}
+
+// Window read: all threads copy the tile of positions [tpos, tpos + TK) of head h from the paged
+// cache into stage `st` with 16-byte cp.async, each warp its TK / 8 consecutive rows from block
+// `blk` (window_block). A half-warp copies one row's K or V plane (contiguous), and each 16-byte
+// chunk lands at its 128-byte-swizzled place in the stage, the layout a TMA box of the far read
+// gives. Rows at or past seq, and all rows when blk is -1, are zero-filled, so no slot that holds
+// no context entry reaches the MMAs. Every thread then arrives on the stage's mbarrier when its
+// copies have landed.
+template <class C>
+__device__ __forceinline__ void issue_window_tile(unsigned char* smem, uint64_t* full, int st, int64_t tpos, int seq,
+                                                  int h, int blk, const FarParams& p) {
+  constexpr int RPW = C::TK / C::NW;  // rows per warp
+  constexpr int CPR = C::HD / 8;      // 16-byte chunks per K (or V) row
+  constexpr int LPP = CPR >= 32 ? 32 : CPR;  // lanes per (row, plane): 16 at hd 128, 32 at hd 256
+  constexpr int STEPS = RPW * 2 * CPR / 32;
+  static_assert(RPW <= 16 && 16 % RPW == 0 && CPR % LPP == 0 && (RPW * 2 * CPR) % 32 == 0, "window tile split");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = warp * RPW;
+  const int64_t pos0 = tpos + row0;
+  // lane -> 16-byte chunk cc of a row; at hd 128 lanes 0-15 copy K and 16-31 copy V of one row per
+  // step, at hd 256 every lane copies one chunk of K, then of V
+  const int cc = lane % LPP;
+  const int lane_plane = LPP == 16 ? lane / 16 : 0;
+  const int64_t slot0 = pos0 - (pos0 / p.block_size) * p.block_size;
+  const int64_t off = blk >= 0 ? static_cast<int64_t>(blk) * p.s_block + h * p.s_head + slot0 * p.s_slot + cc * 8 : 0;
+  const int rows_valid = blk >= 0 ? static_cast<int>(max64(0, min64(RPW, seq - pos0))) : 0;
+  const uint32_t stage = smem_u32(smem + st * C::STAGE_BYTES);
+#pragma unroll 1
+  for (int k = 0; k < STEPS; ++k) {
+    const int plane = LPP == 16 ? lane_plane : (k & 1);
+    const int r = LPP == 16 ? k : (k >> 1);
+    const int row = row0 + r;
+    const bool valid = r < rows_valid;
+    const __nv_bfloat16* src = (plane ? p.vc : p.kc) + (valid ? off + r * p.s_slot : 0);
+    const uint32_t dst = stage + (plane * C::KBOX + (cc >> 3)) * C::BOX_BYTES + row * 128 + (((cc & 7) ^ (row & 7)) << 4);
+    cp_async_16(dst, src, valid ? 16u : 0u);
   }
+  cp_async_mbar_arrive(&full[st]);
 }
 
 // One thread's share of a CTA's query rows for the vectorised rotation: each work item is one
@@ -226,27 +243,37 @@ __device__ __forceinline__ int64_t window_hi(const FarParams& p, int hist, int s
   return max64(hi, 0);
 }
 
-// Zeroes the V rows [from, TK) of a landed stage (window read: positions past the context, whose
-// cache slots may hold anything; their P is 0, but 0 * NaN would not be).
-template <class C>
-__device__ __forceinline__ void zero_v_rows(unsigned char* stage, int from) {
-  const int per_box = (C::TK - from) * 8;  // 16-byte units
-  for (int u = threadIdx.x; u < per_box * C::KBOX; u += C::NTHREADS) {
-    const int x = u / per_box, r = u - x * per_box;
-    *reinterpret_cast<uint4*>(stage + (C::KBOX + x) * C::BOX_BYTES + (from + (r >> 3)) * 128 + (r & 7) * 16) =
-        make_uint4(0u, 0u, 0u, 0u);
-  }
-  fence_proxy_async_shared();  // the stage is refilled by TMA later
+// Far read: the tiles of TK keys this cache holds for the step, the position of tile 0 and the end
+// of the last row's far keys in this cache (row r reads [0, H - W - B + 1 + r)).
+template <int TK>
+__device__ __forceinline__ int far_tiles(const FarParams& p, int hist, int64_t* pos0, int64_t* end) {
+  const int lim_base = hist - p.window - p.block + 1;
+  *end = min64(max(lim_base + p.n - 1, 0), p.pos_lo + p.local_cap);
+  *pos0 = p.pos_lo;
+  const int64_t len = max64(*end - p.pos_lo, 0);
+  return static_cast<int>((len + TK - 1) / TK);
 }
 
-// The split-KV read of one (split, KV head), in two modes.
+// Window read: the tiles of TK positions (aligned to TK) covering the union of the rows' windows,
+// the position of tile 0 and the union's end.
+template <int TK>
+__device__ __forceinline__ int window_tiles(const FarParams& p, int hist, int seq, int64_t* pos0, int64_t* end) {
+  const int64_t u_lo = window_lo(p, hist, 0), u_hi = window_hi(p, hist, seq, p.n - 1);
+  const int64_t t0 = u_lo / TK;
+  *pos0 = t0 * TK;
+  *end = u_hi;
+  return u_hi > u_lo ? static_cast<int>((u_hi + TK - 1) / TK - t0) : 0;
+}
+
+// The split-KV read of one (split of nsplits, KV head h), in two modes.
 //   WIN = false, far memory: K|V rows of the side cache through `map`, the query rotated to the
 //     shared far position, row r reads positions [0, H - W - B + 1 + r) (fold/attention.py:164).
-//   WIN = true, window read: K through `map` and V through `vmap` from the paged cache, the
-//     query as given, row r reads its exact-position window (fold/attention.py:148-151,163).
+//   WIN = true, window read: K and V rows of the paged cache (p.kc, p.vc, cp.async by every
+//     thread), the query as given, row r reads its exact-position window
+//     (fold/attention.py:148-151,163).
 template <class C, bool WIN>
 __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
-                                           int split, int h) {
+                                           int split, int h, int nsplits) {
   constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
   constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
   extern __shared__ unsigned char smem_raw[];
@@ -270,32 +297,27 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   const int qlen = p.qsl[1] - p.qsl[0];
   const int seq = p.seq[0];
   const int hist = max(seq - qlen, 0);
-  int lim_base = 0;  // far: row r reads positions [0, lim_base + r)
-  int64_t end;       // far: end of this cache's keys for the last row
-  int64_t pos0;      // position of tile 0
-  int tiles;
-  if constexpr (!WIN) {
-    lim_base = hist - p.window - p.block + 1;
-    end = min64(max(lim_base + p.n - 1, 0), p.pos_lo + p.local_cap);
-    const int64_t len = max64(end - p.pos_lo, 0);
-    tiles = static_cast<int>((len + TK - 1) / TK);
-    pos0 = p.pos_lo;
-  } else {
-    const int64_t u_lo = window_lo(p, hist, 0), u_hi = window_hi(p, hist, seq, p.n - 1);
-    const int64_t t0 = u_lo / TK;
-    tiles = u_hi > u_lo ? static_cast<int>((u_hi + TK - 1) / TK - t0) : 0;
-    pos0 = t0 * TK;
-    end = u_hi;
-  }
-  const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / p.splits);
-  const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / p.splits) - t_begin;
+  const int lim_base = hist - p.window - p.block + 1;  // far: row r reads positions [0, lim_base + r)
+  int64_t end;   // far: end of this cache's keys for the last row
+  int64_t pos0;  // position of tile 0
+  const int tiles = WIN ? window_tiles<TK>(p, hist, seq, &pos0, &end) : far_tiles<TK>(p, hist, &pos0, &end);
+  const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / nsplits);
+  const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / nsplits) - t_begin;
 
   uint64_t pol = 0;
-  auto issue = [&](int st, int t) {  // tile t of this cache into stage st
-    if constexpr (WIN)
-      issue_window_tile<C>(smem, full, map, vmap, st, pos0 + static_cast<int64_t>(t) * TK, seq, h, p, pol);
-    else
+  // Window read: lane 0 of each warp holds the block of the warp's rows in the next tile to be
+  // issued (looked up one tile ahead, so that the lookup's latency is off the refill's path).
+  int next_blk = -1;
+  // Tile t of this cache into stage st: far read by thread 0 (TMA), window read by every thread.
+  auto issue = [&](int st, int t) {
+    if constexpr (WIN) {
+      const int blk = __shfl_sync(0xffffffffu, next_blk, 0);
+      if (lane == 0 && t + 1 < t_begin + ntiles)
+        next_blk = window_block<C>(p, pos0 + static_cast<int64_t>(t + 1) * TK, seq);
+      issue_window_tile<C>(smem, full, st, pos0 + static_cast<int64_t>(t) * TK, seq, h, blk, p);
+    } else {
       issue_tile<C>(smem, full, map, st, t, p.hkv, h, pol);
+    }
   };
   if (tid == 0) {
     if constexpr (!WIN) {
@@ -306,13 +328,14 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       }
     }
 #pragma unroll
-    for (int i = 0; i < NSTAGE; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < NSTAGE; ++i) mbar_init(&full[i], WIN ? NTH : 1);
     fence_mbar_init();
-    // Fill the ring right away, so the first copies overlap the query rotation below.
-    pol = l2_evict_first_policy();
-    prefetch_tensormap(map);
-    if constexpr (WIN) prefetch_tensormap(vmap);
-    for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
+    if constexpr (!WIN) {
+      // Fill the ring right away, so the first copies overlap the query rotation below.
+      pol = l2_evict_first_policy();
+      prefetch_tensormap(map);
+      for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
+    }
   }
 
   // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table.
@@ -359,6 +382,19 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     }
   }
   __syncthreads();  // barrier inits and the query tile are visible to every warp
+  if constexpr (WIN) {
+    if (ntiles > 0) {
+      // the first tiles' blocks in one round of loads: lane i looks up tile t_begin + i
+      int first = -1;
+      if (lane < NSTAGE + 1 && lane < ntiles)
+        first = window_block<C>(p, pos0 + static_cast<int64_t>(t_begin + lane) * TK, seq);
+      for (int i = 0; i < NSTAGE && i < ntiles; ++i) {
+        const int blk = __shfl_sync(0xffffffffu, first, i);
+        issue_window_tile<C>(smem, full, i, pos0 + static_cast<int64_t>(t_begin + i) * TK, seq, h, blk, p);
+      }
+      next_blk = __shfl_sync(0xffffffffu, first, NSTAGE < 31 ? NSTAGE : 31);
+    }
+  }
 
   // Warp roles.
   const int mt = warp % MT, ng = warp / MT, nt_lo = ng * QNT;  // QK: key m-tile, n-tile group
@@ -428,10 +464,6 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
     const int64_t tpos = pos0 + static_cast<int64_t>(t_begin + it) * TK;  // first position of the tile
     const int64_t key0 = tpos + mt * 16 + g4;
-    if constexpr (WIN) {
-      const int valid = static_cast<int>(max64(0, min64(TK, seq - tpos)));
-      if (ok && valid < TK) zero_v_rows<C>(smem + st * C::STAGE_BYTES, valid);
-    }
 
     float x[QNT][4];
     float ls[QNT][2];
@@ -502,7 +534,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     // One barrier per tile: P^T of every warp is written, every warp is done with the previous
     // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
     const bool attention = named_bar_or(exceed || !ok, 1, NTH);
-    if (tid == 0 && it >= 1 && it - 1 + NSTAGE < ntiles)
+    if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles)
       issue((it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE);
     if (attention) {
       if (named_bar_or(!ok, 2, NTH)) {
@@ -615,7 +647,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   const int64_t l_split = static_cast<int64_t>(split) * p.hq * p.n;
   if (timed_out) {
     // Copies still in flight must land before this CTA's shared memory is released.
-    if (tid == 0) {
+    if constexpr (WIN) {
+      cp_async_wait_all();
+    } else if (tid == 0) {
       const int issued = min(ntiles, max(consumed, 1) - 1 + NSTAGE);
       for (int i = consumed; i < issued; ++i)
         if (!mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1)) break;

@@ -229,36 +229,41 @@ def window_read(q, qsl, seq_lens, k_cache, v_cache, block_table, o_part, lse_par
               _p(o_part), _p(lse_part), splits, n, hq, k_cache.shape[1], d, _p(err), _stream(q))
 
 
-def step_read(q_far, q_win, qsl, seq_lens, side, far_parts, k_cache, v_cache, block_table, window_parts, *, window,
-              block, far_distance, softmax_scale, alpha, window_size, causal, table=None, rot_dim=None,
+def step_read(q_far, q_win, qsl, seq_lens, side, far_parts, k_cache, v_cache, block_table, window_parts, plan, *,
+              window, block, far_distance, softmax_scale, alpha, window_size, causal, table=None, rot_dim=None,
               far_len=None, pos_lo=0, capacity=None, err=None):
     """The far read (as far_read, of q_far) and the window read (as window_read, of q_win) of one
-    draft step in one launch: per KV head the window read's splits run beside the far read's.
-    far_parts and window_parts are (o, lse) split buffers; the far softmax scale is
-    alpha * softmax_scale, the window's softmax_scale."""
+    draft step in one launch: the S blocks of each KV head share the two reads, split per step
+    from the device-side lengths. far_parts and window_parts are (o, lse) buffers of S slots each;
+    the step stores its split (window blocks) in plan (int32 [1], device), which merge_partials
+    reads. The far softmax scale is alpha * softmax_scale, the window's softmax_scale. Not for
+    shapes whose far read takes the tcgen05 kernel (far_read_uses_tcgen05)."""
     (fo_, fl_), (wo_, wl_) = far_parts, window_parts
-    _require_cuda(q_far, q_win, qsl, seq_lens, side, fo_, fl_, k_cache, v_cache, block_table, wo_, wl_, table,
+    _require_cuda(q_far, q_win, qsl, seq_lens, side, fo_, fl_, k_cache, v_cache, block_table, wo_, wl_, plan, table,
                   far_len, err)
     _check_lengths(qsl, seq_lens)
     n, hq, d = q_far.shape
     if q_win.shape != q_far.shape:
         raise FoldError("step_read: the far and window queries must have the same shape")
-    fsplits = _check_partials(fo_, fl_, n, hq, d, "step_read")
-    wsplits = _check_partials(wo_, wl_, n, hq, d, "step_read")
+    splits = _check_partials(fo_, fl_, n, hq, d, "step_read")
+    if _check_partials(wo_, wl_, n, hq, d, "step_read") != splits:
+        raise FoldError("step_read: the far and window partials must have the same number of slots")
+    if plan.dtype != torch.int32 or plan.numel() < 1:
+        raise FoldError("step_read: plan must be an int32 tensor of at least one element")
     q_far, side_args = _side_args(q_far, side, table, rot_dim, pos_lo, capacity, far_len)
     q_win, paged = _paged_args(q_win, k_cache, v_cache, block_table, window_size, causal)
     _lib.call("fold_step_read", _p(q_far), q_far.stride(0), q_far.stride(1), _p(q_win), q_win.stride(0),
-              q_win.stride(1), _p(qsl), _p(seq_lens), *side_args, _p(fo_), _p(fl_), fsplits, *paged, _p(wo_), _p(wl_),
-              wsplits, n, hq, side.shape[1], d, int(window), int(block), int(far_distance),
+              q_win.stride(1), _p(qsl), _p(seq_lens), *side_args, _p(fo_), _p(fl_), *paged, _p(wo_), _p(wl_),
+              splits, _p(plan), n, hq, side.shape[1], d, int(window), int(block), int(far_distance),
               float(softmax_scale) * float(alpha), float(softmax_scale), _p(err), _stream(q_far))
 
 
-def merge_partials(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens, *, window, block, alpha):
+def merge_partials(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens, *, window, block, alpha, plan=None):
     """Writes into out [n, Hq, D] bf16 the alpha-weighted merge (fold/kernels.py:135-142) of the
     window read's split partials (o_wpart [Sw, n, Hq, D], lse_wpart [Sw, Hq, n]) with the far
     read's (o_fpart [Sf, n, Hq, D], lse_fpart [Sf, Hq, n]); with o_fpart None the combined window
-    read alone."""
-    _require_cuda(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens)
+    read alone. With `plan` (step_read's device word) only the slots that step used are read."""
+    _require_cuda(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens, plan)
     _check_lengths(qsl, seq_lens)
     sw, n, hq, d = o_wpart.shape
     sf = 0 if o_fpart is None else o_fpart.shape[0]
@@ -270,8 +275,10 @@ def merge_partials(o_wpart, lse_wpart, o_fpart, lse_fpart, out, qsl, seq_lens, *
             raise FoldError("merge_partials: partials must be contiguous float32 [S, n, Hq, D] and [S, Hq, n]")
     if out.dtype != torch.bfloat16 or out.stride(-1) != 1 or out.shape != (n, hq, d):
         raise FoldError("merge_partials: out must be bfloat16 [n, Hq, D] with a contiguous head dimension")
-    _lib.call("fold_merge_partials", _p(o_wpart), _p(lse_wpart), sw, _p(o_fpart), _p(lse_fpart), sf, _p(out),
-              out.stride(0), out.stride(1), _p(qsl), _p(seq_lens), n, hq, d, int(window), int(block),
+    if plan is not None and (plan.dtype != torch.int32 or sf != sw):
+        raise FoldError("merge_partials: a step plan is int32, with both partial sets of the same slot count")
+    _lib.call("fold_merge_partials", _p(o_wpart), _p(lse_wpart), sw, _p(o_fpart), _p(lse_fpart), sf, _p(plan),
+              _p(out), out.stride(0), out.stride(1), _p(qsl), _p(seq_lens), n, hq, d, int(window), int(block),
               1.0 / float(alpha), _stream(out))
 
 
@@ -334,6 +341,11 @@ def select_far_read_kernel(kernel: str = "auto") -> None:
     if kernel not in FAR_READ_KERNELS:
         raise FoldError(f"far-read kernel must be one of {sorted(FAR_READ_KERNELS)}")
     _lib.call("fold_far_read_select_kernel", FAR_READ_KERNELS[kernel])
+
+
+def far_read_uses_tcgen05(hd, n, hq, hkv) -> bool:
+    """Whether the far read of this shape takes the tcgen05 kernel (no one-launch step read then)."""
+    return _lib.far_read_kernel_for(hd, n, hq, hkv) == 1
 
 
 def default_splits(hkv):

@@ -130,30 +130,35 @@ int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
 
 /* The far read and the window read of one draft step in one launch. Replaces, for a full-attention
  * FOLD layer, far_query + both FlashAttention reads of fold/attention.py:162-170. Arguments as
- * fold_far_read (q_far, the rope table, the side cache, far_len, the far partials o_fpart/lse_fpart
- * with fsplits splits, far_scale = alpha * scale) and as fold_window_read (q_win, the paged cache,
- * its block table, the window, the window partials o_wpart/lse_wpart with wsplits splits,
- * win_scale = scale). The launch's blocks are hkv * fsplits far-read blocks followed by
- * hkv * wsplits window-read blocks, so the window read (a few MB) runs beside the far read instead
- * of after it. Keep hkv * (fsplits + wsplits) within one block per SM (e.g. wsplits = 1,
- * fsplits = fold_far_read_default_splits - 1): blocks beyond the device may start only when far
- * blocks finish. When the far read takes the tcgen05 kernel (see fold_far_read_select_kernel) the
- * two reads are issued as two launches. Merge the result with fold_merge_partials. */
+ * fold_far_read (q_far, the rope table, the side cache, far_len, the far partials o_fpart/lse_fpart,
+ * far_scale = alpha * scale) and as fold_window_read (q_win, the paged cache, its block table, the
+ * window, the window partials o_wpart/lse_wpart, win_scale = scale). `splits` blocks per KV head
+ * (at least 2; fold_far_read_default_splits, one block per SM in all, keeps the launch one wave)
+ * share the two reads: from the device-side lengths each step picks w, the number that read the
+ * window, so that the window read (a few MB) runs beside the far read instead of after it. The
+ * window read fills window slots [0, w) and the far read far slots [0, splits - w) of partial sets
+ * of `splits` slots each; the step stores w in plan[0] (a device int), which fold_merge_partials
+ * reads. Shapes whose far read takes the tcgen05 kernel (fold_far_read_kernel_for) fail with
+ * FOLD_ERR_UNSUPPORTED: issue fold_far_read and fold_window_read for them. */
 int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_head, const void* q_win,
                    int64_t qw_stride_tok, int64_t qw_stride_head, const int* qsl, const int* seq_lens,
                    const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
-                   int64_t capacity, int* far_len, float* o_fpart, float* lse_fpart, int fsplits,
-                   const void* k_cache, const void* v_cache, int64_t num_blocks, int block_size,
-                   int64_t cache_stride_block, int64_t cache_stride_head, int64_t cache_stride_slot,
-                   const int* block_table, int block_table_len, int window_left, int window_right, int causal,
-                   float* o_wpart, float* lse_wpart, int wsplits, int n, int hq, int hkv, int hd, int window,
-                   int block, int far_distance, float far_scale, float win_scale, int* err, void* stream);
+                   int64_t capacity, int* far_len, float* o_fpart, float* lse_fpart, const void* k_cache,
+                   const void* v_cache, int64_t num_blocks, int block_size, int64_t cache_stride_block,
+                   int64_t cache_stride_head, int64_t cache_stride_slot, const int* block_table, int block_table_len,
+                   int window_left, int window_right, int causal, float* o_wpart, float* lse_wpart, int splits,
+                   int* plan, int n, int hq, int hkv, int hd, int window, int block, int far_distance, float far_scale,
+                   float win_scale, int* err, void* stream);
 
 /* Chooses the far-read kernel for later calls: 0 = mma.sync tiles, 1 = tcgen05 tiles with TMEM
  * accumulators, -1 = per shape (the default: tcgen05 above 48 query rows per KV head). Both give
  * the same results within rounding. The environment variable FOLD_FAR_READ_KERNEL=mma|tc sets
  * the initial choice. No reference counterpart (a tuning switch of this implementation). */
 int fold_far_read_select_kernel(int kernel);
+
+/* The far-read kernel later calls take for this shape: 0 = mma.sync tiles, 1 = tcgen05 tiles,
+ * -1 = invalid sizes. No reference counterpart. */
+int fold_far_read_kernel_for(int hd, int n, int hq, int hkv);
 
 /* Split count that fills the device for `hkv` KV heads (one CTA per SM). */
 int fold_far_read_default_splits(int hkv, int hd, int n, int hq);
@@ -178,9 +183,11 @@ int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, c
  * by fold_window_read) and the far read's fsplits partials (as written by fold_far_read) are each
  * combined by log-sum-exp, then merged with the alpha weighting of fold_merge. fsplits = 0 (far
  * pointers may then be NULL) writes the combined window read alone (the window ablation and plain
- * sliding layers). All partials float32 and contiguous; out bf16 with strides (tok, head). */
+ * sliding layers). `plan` (may be NULL) is fold_step_read's device word: then wsplits == fsplits
+ * and the window set uses its first plan[0] slots, the far set its first wsplits - plan[0]. All
+ * partials float32 and contiguous; out bf16 with strides (tok, head). */
 int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplits, const float* o_fpart,
-                        const float* lse_fpart, int fsplits, void* out, int64_t out_stride_tok,
+                        const float* lse_fpart, int fsplits, const int* plan, void* out, int64_t out_stride_tok,
                         int64_t out_stride_head, const int* qsl, const int* seq_lens, int n, int hq, int hd,
                         int window, int block, float inv_alpha, void* stream);
 

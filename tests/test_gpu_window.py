@@ -148,24 +148,41 @@ def test_merge_partials_matches_oracle_fold_step(hist):
     kernels.merge_partials(wo, wl, fo_p, fl_p, out, qsl, seq_t, window=W, block=B, alpha=alpha)
     torch.cuda.synchronize()
     assert np.abs(to64(out) - want).max() <= OUT_ATOL
+    # the same step as one launch of both reads (the blocks split per step) and the merge of the
+    # slots the step used
+    S = kernels.default_splits(hkv)
+    far = (torch.empty((S, n, hq, hd), device="cuda"), torch.empty((S, hq, n), device="cuda"))
+    win = (torch.empty((S, n, hq, hd), device="cuda"), torch.empty((S, hq, n), device="cuda"))
+    plan = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kernels.step_read(qd, qd, qsl, seq_t, side, far, kc, vc, table, win, plan, window=W, block=B, far_distance=W + B,
+                      softmax_scale=scale, alpha=alpha, window_size=(W + B - 1, B - 1), causal=False, table=tab)
+    out2 = torch.empty_like(out)
+    kernels.merge_partials(win[0], win[1], far[0], far[1], out2, qsl, seq_t, window=W, block=B, alpha=alpha,
+                           plan=plan)
+    torch.cuda.synchronize()
+    assert 1 <= int(plan.item()) < S
+    assert np.abs(to64(out2) - want).max() <= OUT_ATOL
 
 
-@pytest.mark.parametrize("hd,hq,hkv,n,hist", [(128, 32, 8, 10, 20000), (256, 16, 8, 8, 9000), (256, 16, 4, 16, 7000)])
+@pytest.mark.parametrize("hd,hq,hkv,n,hist", [(128, 32, 8, 10, 20000), (128, 32, 8, 10, 131062),
+                                              (128, 32, 8, 8, 32760), (256, 16, 8, 8, 9000)])
 def test_step_read_equals_separate_reads(hd, hq, hkv, n, hist, far_kernel):
-    """The one-launch step read writes bit for bit the partials of fold_far_read and
-    fold_window_read with the same split counts (or, with the tcgen05 far read, issues those two
-    launches)."""
+    """The one-launch step read splits each KV head's S blocks into w window and S - w far blocks
+    (plan[0] = w) and writes bit for bit the partials of fold_window_read with w splits and of
+    fold_far_read with S - w splits. Shapes whose far read takes the tcgen05 kernel are refused."""
+    from fold_b200.errors import FoldError
+
     rng = np.random.default_rng(hd + hist)
     W, B, alpha = 2048, n, 2.0
     seq = hist + n
     f = fo.inv_freq(500000.0, hd)
     qd = bf16_tensor(rng.standard_normal((n, hq, hd)))
-    k_raw = rng.standard_normal((seq, hkv, hd))
-    v = rng.standard_normal((seq, hkv, hd))
+    k_raw = rng.standard_normal((seq, hkv, hd), dtype=np.float32)
+    v = rng.standard_normal((seq, hkv, hd), dtype=np.float32)
     kv, table = paged_from(k_raw, v, 16, rng)
     side = side_from(k_raw, v, fo.side_pages(seq))
     from fold_b200.rope import rope_table
-    tab = rope_table(torch.from_numpy(f), 1 << 16, "cuda")
+    tab = rope_table(torch.from_numpy(f), 1 << 18, "cuda")
     qsl, seq_t = lengths(n, hist)
     kc, vc = kernels.paged_planes(kv, hd)
     scale = hd ** -0.5
@@ -175,14 +192,24 @@ def test_step_read_equals_separate_reads(hd, hq, hkv, n, hist, far_kernel):
         return (torch.full((s, n, hq, hd), float("nan"), device="cuda"),
                 torch.full((s, hq, n), float("nan"), device="cuda"))
 
-    fs = kernels.default_splits(hkv)  # one far block per SM: the window blocks overflow the device
-    far_a, win_a, far_b, win_b = bufs(fs), bufs(1), bufs(fs), bufs(1)
-    kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, window=W, block=B, far_distance=W + B,
-                      softmax_scale=scale, alpha=alpha, window_size=ws, causal=False, table=tab)
+    S = kernels.default_splits(hkv)
+    far_a, win_a = bufs(S), bufs(S)
+    plan = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = dict(window=W, block=B, far_distance=W + B, softmax_scale=scale, alpha=alpha, window_size=ws,
+                causal=False, table=tab)
+    if kernels.far_read_uses_tcgen05(hd, n, hq, hkv):
+        with pytest.raises(FoldError, match="tcgen05"):
+            kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, plan, **args)
+        return
+    kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, plan, **args)
+    torch.cuda.synchronize()
+    w = int(plan.item())
+    assert 1 <= w < S
+    far_b, win_b = bufs(S - w), bufs(w)
     kernels.far_read(qd, qsl, seq_t, side, far_b[0], far_b[1], window=W, block=B, far_distance=W + B,
                      softmax_scale=scale * alpha, table=tab)
     kernels.window_read(qd, qsl, seq_t, kc, vc, table, win_b[0], win_b[1], window_size=ws, causal=False,
                         softmax_scale=scale)
     torch.cuda.synchronize()
-    for a, b in zip(far_a + win_a, far_b + win_b):
-        assert torch.equal(a, b)
+    assert torch.equal(far_a[0][: S - w], far_b[0]) and torch.equal(far_a[1][: S - w], far_b[1])
+    assert torch.equal(win_a[0][:w], win_b[0]) and torch.equal(win_a[1][:w], win_b[1])
