@@ -165,7 +165,8 @@ def test_merge_partials_matches_oracle_fold_step(hist):
 
 
 @pytest.mark.parametrize("hd,hq,hkv,n,hist", [(128, 32, 8, 10, 20000), (128, 32, 8, 10, 131062),
-                                              (128, 32, 8, 8, 32760), (256, 16, 8, 8, 9000)])
+                                              (128, 32, 8, 8, 32760), (256, 16, 8, 8, 9000),
+                                              (128, 32, 8, 10, 1500)])  # last: no far key at all
 def test_step_read_equals_separate_reads(hd, hq, hkv, n, hist, far_kernel):
     """The one-launch step read splits each KV head's S blocks into w window and S - w far blocks
     (plan[0] = w) and writes bit for bit the partials of fold_window_read with w splits and of
