@@ -102,3 +102,78 @@ def test_binding_argument_types_match_header():
                 assert t is not ctypes.c_int and t is not ctypes.c_float, (name, p)
             else:
                 assert t is want, (name, p, t)
+
+
+def test_far_read_kernel_choice_per_shape():
+    from fold_b200 import kernels
+    kernels.select_far_read_kernel("auto")
+    try:
+        # mma.sync tiles up to 48 query rows per KV head, tcgen05 tiles past that
+        assert _lib.far_read_kernel_for(128, 8, 32, 8) == 0      # 32 rows
+        assert _lib.far_read_kernel_for(256, 8, 16, 8) == 0      # 16 rows
+        assert _lib.far_read_kernel_for(128, 12, 32, 8) == 0     # 48 rows
+        assert _lib.far_read_kernel_for(128, 16, 32, 8) == 1     # 64 rows
+        assert kernels.far_read_uses_tcgen05(128, 16, 32, 8)
+        assert _lib.far_read_kernel_for(128, 8, 32, 5) == -1     # hq not a multiple of hkv
+        assert _lib.far_read_kernel_for(128, 0, 32, 8) == -1
+        kernels.select_far_read_kernel("mma")
+        assert _lib.far_read_kernel_for(128, 16, 32, 8) == 0
+        kernels.select_far_read_kernel("tc")
+        assert _lib.far_read_kernel_for(128, 8, 32, 8) == 1
+    finally:
+        kernels.select_far_read_kernel("auto")
+
+
+# Stand-in addresses that pass the alignment checks; every case below fails validation before
+# any CUDA call, so nothing is dereferenced.
+_P = 1 << 20
+
+
+def _window_args(**kw):
+    a = dict(q=_P, qst=4096, qsh=128, qsl=_P, seq=_P, kc=_P, vc=_P, num_blocks=64, block_size=16, sb=32768,
+             sh=2048, ss=128, bt=_P, bt_len=8, wl=2063, wr=15, causal=1, scale=0.088, o=_P, lse=_P, splits=18,
+             n=8, hq=32, hkv=8, hd=128, err=None, stream=None)
+    a.update(kw)
+    return list(a.values())
+
+
+def test_window_read_rejects_bad_arguments_without_a_gpu():
+    with pytest.raises(FoldError, match="window read: null pointer"):
+        _lib.call("fold_window_read", *_window_args(bt=None))
+    with pytest.raises(FoldError, match="head size"):
+        _lib.call("fold_window_read", *_window_args(hd=64))
+    with pytest.raises(FoldError, match="block size"):
+        _lib.call("fold_window_read", *_window_args(block_size=8))
+    with pytest.raises(FoldError, match="16-byte aligned"):
+        _lib.call("fold_window_read", *_window_args(ss=100))
+    with pytest.raises(FoldError, match="bad sizes"):
+        _lib.call("fold_window_read", *_window_args(hkv=5))
+    with pytest.raises(FoldError, match="at most 64"):
+        _lib.call("fold_window_read", *_window_args(n=32))
+
+
+def test_step_read_requires_a_plan_word():
+    with pytest.raises(FoldError, match="step read: null plan"):
+        # every pointer null and every size zero: the plan word is checked first
+        args = [None if t is ctypes.c_void_p else 0 for t in _lib.SIGNATURES["fold_step_read"]]
+        _lib.call("fold_step_read", *args)
+
+
+def test_merge_partials_rejects_bad_arguments_without_a_gpu():
+    base = [_P, _P, 18, _P, _P, 18, None, _P, 4096, 128, _P, _P, 8, 32, 128, 2048, 16, 0.5, None]
+    with pytest.raises(FoldError, match="same slot count"):
+        args = list(base)
+        args[5], args[6] = 17, _P
+        _lib.call("fold_merge_partials", *args)
+    with pytest.raises(FoldError, match="head size"):
+        args = list(base)
+        args[14] = 130
+        _lib.call("fold_merge_partials", *args)
+    with pytest.raises(FoldError, match="null pointer"):
+        args = list(base)
+        args[3] = None
+        _lib.call("fold_merge_partials", *args)
+    with pytest.raises(FoldError, match="element pairs"):
+        args = list(base)
+        args[8] = 4095
+        _lib.call("fold_merge_partials", *args)
