@@ -156,3 +156,79 @@ def test_single_rank_far_read_exchange_equals_far_read_and_merge(n, hq, hkv, hd,
         del graph
     finally:
         ex.close()
+
+
+def _silent_peer_worker(rank, port, q):
+    """Rank 0 merges through a two-rank exchange whose rank 1 never takes the step (both ranks on
+    cuda:0; rank 1 only maps its region and waits on the host). Rank 0's wait for rank 1's record
+    runs out after its bounded limit, the kernel records the timeout and merges what it has."""
+    import os
+    import time
+
+    import torch.distributed as dist
+
+    from fold_b200.errors import DEVERR_TIMEOUT
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(0)
+    ex = None
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        S, n, hq, hd, W, B, hist = 6, 4, 8, 128, 2048, 4, 9000
+        ex = PeerExchange(n=n, hq=hq, hd=hd)
+        result = None
+        if rank == 0:
+            o, lse, o_l, lse_l = partials(7, S, n, hq, hd)
+            qsl = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+            seq = torch.tensor([hist + n], dtype=torch.int32, device="cuda")
+            err = torch.zeros(1, dtype=torch.int32, device="cuda")
+            out = torch.empty((n, hq, hd), dtype=torch.bfloat16, device="cuda")
+            times, words = [], []
+            for _ in range(2):
+                err.zero_()
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                ex.merge(o, lse, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=2.0, err=err)
+                torch.cuda.synchronize()
+                times.append(time.perf_counter() - t0)
+                words.append(int(err.item()))
+            # the context is still usable: the plain merge of the same partials runs and agrees
+            want = torch.empty_like(out)
+            kernels.merge(o_l, lse_l, o, lse, want, qsl, seq, window=W, block=B, alpha=2.0)
+            torch.cuda.synchronize()
+            result = (times, words, DEVERR_TIMEOUT, to64(out), to64(want))
+        ex.close()  # both ranks meet here, after rank 0's launches have finished
+        ex = None
+        q.put((rank, "ok", result))
+    except Exception as e:
+        q.put((rank, "error", repr(e)))
+    finally:
+        if ex is not None:
+            ex.close()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_exchange_wait_runs_out_when_a_peer_never_merges():
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_silent_peer_worker, args=(r, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = dict((r, (st, x)) for r, st, x in (q.get(timeout=300) for _ in range(2)))
+    for pr in procs:
+        pr.join(timeout=60)
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    times, words, timeout_bit, out, want = res[0][1]
+    # first launch: the wait gives up after its 2 s limit; second: the exchange is poisoned and
+    # the launch does not wait at all
+    assert all(w & timeout_bit for w in words), words
+    assert 1.5 <= times[0] <= 30.0, times
+    assert times[1] < 1.0, times
+    # with the peer's partial missing, the output is this rank's own merge
+    np.testing.assert_array_equal(out, want)
