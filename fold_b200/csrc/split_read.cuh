@@ -433,6 +433,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         lim[j][c] = valid ? static_cast<int>(min64(lim_base + rho / G, end)) : 0;
       }
     }
+  // Far read: the row limits grow with the row, so a tile that ends at or below row 0's limit is
+  // visible to every query row. Its logits skip the per-key test; the padding rows of the last
+  // n-tile (limit 0) still get -inf (their Q rows are zero, so their products are 0).
+  const int64_t open_end = WIN ? 0 : min64(lim_base, end);
 
   float oacc[PV_MT][NT][4];
 #pragma unroll
@@ -496,17 +500,29 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         }
       }
       // ---- scale, mask, exponentiate against the current row maximum
+      if (!WIN && tpos + TK <= open_end) {
 #pragma unroll
-      for (int j = 0; j < QNT; ++j) {
+        for (int j = 0; j < QNT; ++j) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = e & 1;
-          const int64_t key = key0 + (e >> 1) * 8;
-          bool vis = key < lim[j][c];
-          if constexpr (WIN) vis = vis && key >= llo[j][c];
-          const float v = vis ? x[j][e] * p.scale_log2 : -INFINITY;
-          x[j][e] = v;
-          exceed |= v > MQ(j, c) + kRaise;
+          for (int e = 0; e < 4; ++e) {
+            const float v = fmaf(x[j][e], p.scale_log2, lim[j][e & 1] > 0 ? 0.f : -INFINITY);
+            x[j][e] = v;
+            exceed |= v > MQ(j, e & 1) + kRaise;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < QNT; ++j) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = e & 1;
+            const int64_t key = key0 + (e >> 1) * 8;
+            bool vis = key < lim[j][c];
+            if constexpr (WIN) vis = vis && key >= llo[j][c];
+            const float v = vis ? x[j][e] * p.scale_log2 : -INFINITY;
+            x[j][e] = v;
+            exceed |= v > MQ(j, c) + kRaise;
+          }
         }
       }
       if (it == 0) {
