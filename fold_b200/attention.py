@@ -241,10 +241,7 @@ class _Wrapped:
             kernels.merge_partials(win[0], win[1], far[0], far[1], out, qsl, seq, window=w.window, block=w.block,
                                    alpha=w.alpha, plan=w.plan)
             return
-        if rotate:
-            far = w.read_far(q_far, qsl, seq, o.scale)
-        else:
-            far = w.read_far(q_far, qsl, seq, o.scale, rotate=False)
+        far = w.read_far(q_far, qsl, seq, o.scale, rotate=rotate)
         parts = None if self.local_read is not None else w.window_partials(n, hq)
         self._window_and_merge(q_win, kv_cache, meta, parts, far, out, **local)
 
@@ -292,8 +289,8 @@ class NativeWindowAttention(_Wrapped):
 
     def check(self) -> None:
         """Raises FoldError if the window read recorded a device-side error (synchronises)."""
-        if self.err is not None and int(self.err.item()):
-            word = int(self.err.item())
+        word = int(self.err.item()) if self.err is not None else 0
+        if word:
             self.err.zero_()
             raise FoldError(f"FOLD device error: {describe_device_error(word)}")
 
