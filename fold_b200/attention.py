@@ -24,7 +24,6 @@ are memory entries, read from the side cache with the query rotated to the share
 from __future__ import annotations
 
 import copy
-import math
 from types import MethodType
 from typing import Any, Callable, Optional
 
@@ -198,14 +197,10 @@ def _partial_buffers(cache: dict, splits: int, n: int, num_heads: int, head_dim:
 
 
 def logn_scale_rows(q, query_start_loc, seq_lens, logn_ref):
-    """ReRoPE query scale max(1, log(p + 1) / log(ref)) at the absolute position p of each row
-    (fold/attention.py:76-83)."""
-    n = q.shape[0]
-    qlen = query_start_loc[1:2] - query_start_loc[0:1]
-    hist = (seq_lens[0:1] - qlen).clamp_min(0)
-    pos = hist.to(torch.float32) + torch.arange(n, device=q.device, dtype=torch.float32)
-    s = (torch.log(pos + 1.0) / math.log(logn_ref)).clamp_min(1.0)
-    return (q.float() * s[:, None, None]).to(q.dtype)
+    """The ReRoPE query scale max(1, log(p + 1) / log(ref)) at the absolute position p = H + r of
+    each row r (fold/attention.py:76-83), as one kernel (kernels.logn_scale) that reads H from the
+    device-side lengths."""
+    return kernels.logn_scale(q, query_start_loc, seq_lens, logn_ref)
 
 
 LocalRead = Callable[..., Any]

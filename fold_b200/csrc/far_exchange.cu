@@ -83,7 +83,6 @@ template <int NW>
 __device__ __noinline__ void exchange_tail(const FarParams& p, const TailParams& t, int split, int h) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t* done = t.ex.done;  // zero at the start of every launch: its last CTA resets it
-  const uint32_t* poisoned = t.ex.ctr + 2;
   // the previous launch's last block stored ctr[0] (read here, not before the far read, so that
   // the far read's loop keeps all its registers)
   const uint32_t epoch = ld_relaxed_gpu(t.ex.ctr) + 1;
@@ -93,9 +92,11 @@ __device__ __noinline__ void exchange_tail(const FarParams& p, const TailParams&
     atomicAdd(done + h, 1u);
     bool ok = true;
     const uint64_t t0 = globaltimer();
+    // This rank's own splits: the cooperative launch keeps every CTA resident, so they finish.
+    // Only the timer and the poll bound end this wait; a poisoned exchange (a peer that stopped
+    // answering) must not cut it short, or the combine below would read partials still in flight.
     for (uint32_t it = 0; ld_acquire_gpu(done + h) < static_cast<uint32_t>(p.splits); ++it) {
-      if (it >= kPeerWaitMaxPolls || ((it & 31u) == 31u && (ld_relaxed_gpu(poisoned) ||
-                                                            globaltimer() - t0 > kPeerWaitTimeoutNs))) {
+      if (it >= kPeerWaitMaxPolls || ((it & 31u) == 31u && globaltimer() - t0 > kPeerWaitTimeoutNs)) {
         ok = false;
         break;
       }
@@ -147,7 +148,7 @@ struct FarExchangeLaunch {
     CUtensorMap map;
     if (int s = side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)) return s;
     auto kern = far_exchange_kernel<C>;
-    static bool configured = false;  // per instantiation
+    static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(kern, C::SMEM, configured, "cudaFuncSetAttribute(far_exchange)")) return e;
     static int resident = 0;  // CTAs of this instantiation the device holds at once (per process, one device type)
     if (!resident) {

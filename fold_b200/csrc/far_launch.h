@@ -51,13 +51,4 @@ int with_mma_config(int hd, int rows, const F& f) {
   return with_row_tiles<256, 64, 8>(nt, f);
 }
 
-template <class K>
-int allow_smem(K kern, int bytes, bool& configured, const char* what) {
-  if (configured) return FOLD_OK;
-  if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what))
-    return s;
-  configured = true;
-  return FOLD_OK;
-}
-
 }  // namespace fold

@@ -187,7 +187,7 @@ struct FarLaunch {
     const int s = cached_map ? side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)
                              : side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map);
     if (s) return s;
-    static bool configured = false;  // per instantiation
+    static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(far_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(far_read)")) return e;
     far_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
     return check_launch("far_read_kernel");
@@ -199,7 +199,7 @@ struct WindowLaunch {
   cudaStream_t stream;
   template <class C>
   int run() const {
-    static bool configured = false;  // per instantiation
+    static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(window_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(window_read)")) return e;
     window_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(prm);
     return check_launch("window_read_kernel");
@@ -217,7 +217,7 @@ struct StepLaunch {
   int run() const {
     CUtensorMap map;
     if (int s = side_tensor_map(side, pages, far.hkv, C::HD, C::TK, &map)) return s;
-    static bool configured = false;  // per instantiation
+    static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(step_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(step_read)")) return e;
     step_read_kernel<C><<<dim3(far.splits, far.hkv), C::NTHREADS, C::SMEM, stream>>>(map, far, win, plan);
     return check_launch("step_read_kernel");

@@ -15,7 +15,8 @@
 namespace fold {
 
 // 16 MiB of float32 scratch per GPU: split partials o [splits, n, hq, hd] followed by their
-// LSEs [splits, hq, n]. Every GPU that loads the library holds it until the process exits.
+// LSEs [splits, hq, n]. A GPU holds it from the library's first use on that device (with lazy
+// module loading, the first kernel call or symbol lookup there) until the process exits.
 constexpr int64_t kStaticScratchFloats = int64_t(4) << 20;
 
 static __device__ __align__(256) float g_far_scratch[kStaticScratchFloats];

@@ -679,13 +679,8 @@ int launch_tc(const FarParams& prm, const void* side, int pages, bool cached, cu
                        : side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map);
   if (s) return s;
   auto kern = far_read_tc_kernel<C>;
-  static bool configured = false;  // per instantiation
-  if (!configured) {
-    if (int e = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                           "cudaFuncSetAttribute(far_read_tc)"))
-      return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
+  if (int e = allow_smem(kern, C::SMEM, configured, "cudaFuncSetAttribute(far_read_tc)")) return e;
   kern<<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
   return check_launch("far_read_tc_kernel");
 }

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/fold_b200.h"
@@ -30,6 +31,22 @@ int side_tensor_map(const void* side, int pages, int hkv, int hd, int box_rows, 
 int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out);
 
 int device_sm_count();
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device. The attribute
+// belongs to the device's context, so `configured` keeps one bit per device ordinal (< 64; any
+// higher ordinal sets the attribute on every call). Safe to call from several host threads: a
+// race only repeats the idempotent attribute call.
+template <class K>
+int allow_smem(K kern, int bytes, std::atomic<uint64_t>& configured, const char* what) {
+  int dev = 0;
+  if (int s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return s;
+  const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (configured.load(std::memory_order_acquire) & bit)) return FOLD_OK;
+  if (int s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what))
+    return s;
+  if (bit) configured.fetch_or(bit, std::memory_order_release);
+  return FOLD_OK;
+}
 
 // Far read into caller-given partial buffers with the descriptor built on the stack; the
 // arguments and checks are those of fold_far_read.

@@ -1,4 +1,6 @@
-// Far-query rotation and the ReRoPE query pair (fold/kernels.py:21-83 of the reference).
+// Far-query rotation and the ReRoPE query pair (fold/kernels.py:21-83 of the reference), and the
+// ReRoPE query scale alone (fold/attention.py:76-83, logn_scale_rows): fold_rerope_query without
+// a far query and table writes only the scaled query.
 //
 // One CTA per (row, head); thread d computes output element d from q[d] and its neox partner.
 // cos/sin come from a float32 table formed in float64 (rows = |offset|, vLLM cos_sin_cache
@@ -35,7 +37,7 @@ __global__ void rotate_kernel(const RotParams p) {
   int off = p.far_distance - hist - (p.constant ? t : 0);
   const float sgn = off < 0 ? -1.f : 1.f;
   int ad = off < 0 ? -off : off;
-  if (ad >= p.table_rows) {
+  if (p.qf && ad >= p.table_rows) {
     if (threadIdx.x == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
     ad = p.table_rows - 1;
   }
@@ -43,10 +45,11 @@ __global__ void rotate_kernel(const RotParams p) {
   if (p.inv_log_ref > 0.f) sc = fmaxf(logf(static_cast<float>(hist + t + 1)) * p.inv_log_ref, 1.f);
   const int RH = p.rot_dim >> 1;
   const __nv_bfloat16* qr = p.q + t * p.q_st + h * p.q_sh;
-  const float* trow = p.table + static_cast<int64_t>(ad) * p.rot_dim;
+  const float* trow = p.qf ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
   for (int d = threadIdx.x; d < p.hd; d += blockDim.x) {
     const float x = __bfloat162float(qr[d]) * sc;
     if (p.qs) p.qs[t * p.qs_st + h * p.qs_sh + d] = __float2bfloat16_rn(x);
+    if (!p.qf) continue;  // the query scale alone
     float y = x;
     if (d < 2 * RH) {
       const bool lo = d < RH;
@@ -99,8 +102,15 @@ int fold_rerope_query(const void* q, int64_t q_stride_tok, int64_t q_stride_head
                       int* far_len, int n, int hq, int hd, int window, int block, int far_distance, int constant,
                       float inv_log_ref, int* err, void* stream) {
   using namespace fold;
-  if (int s = check_rot_args(q, qf, qsl, seq_lens, rope_table, table_rows, rot_dim, n, hq, hd)) return s;
   if (!qs) return fail(FOLD_ERR_INVALID_ARGUMENT, "rerope: null qs");
+  if (!qf && !rope_table) {  // the query scale alone: qs only
+    if (!q || !qsl || !seq_lens) return fail(FOLD_ERR_INVALID_ARGUMENT, "rerope: null pointer");
+    if (n < 1 || hq < 1 || hd < 1 || static_cast<int64_t>(n) * hq > 2147483647)
+      return fail(FOLD_ERR_INVALID_ARGUMENT, "rerope: bad sizes");
+    rot_dim = 2, table_rows = 1;
+  } else if (int s = check_rot_args(q, qf, qsl, seq_lens, rope_table, table_rows, rot_dim, n, hq, hd)) {
+    return s;
+  }
   RotParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q), p.q_st = q_stride_tok, p.q_sh = q_stride_head;
   p.qs = static_cast<__nv_bfloat16*>(qs), p.qs_st = qs_stride_tok, p.qs_sh = qs_stride_head;

@@ -87,6 +87,28 @@ def rerope_queries(q, qsl, seq_lens, inv_freq, far_len, *, far_distance, window,
     return qs, qf
 
 
+def logn_scale(q, qsl, seq_lens, logn_ref):
+    """q [n, Hq, D] -> q * max(1, log(H + r + 1) / log(logn_ref)) for row r at position H + r,
+    the ReRoPE query scale of fold/attention.py:76-83 (the query-scale path of fold_rerope_query;
+    the step lengths are read on the device)."""
+    _require_cuda(q, qsl, seq_lens)
+    _check_lengths(qsl, seq_lens)
+    if not logn_ref or logn_ref <= 1:
+        raise FoldError("logn_scale: logn_ref must be greater than 1")
+    n, hq, d = q.shape
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    qs = torch.empty((n, hq, d), device=q.device, dtype=q.dtype)
+    if n == 0:
+        return qs
+    if q.dtype != torch.bfloat16:
+        raise FoldError("logn_scale: q must be bfloat16")
+    _lib.call("fold_rerope_query", _p(q), q.stride(0), q.stride(1), _p(qs), qs.stride(0), qs.stride(1), None, 0, 0,
+              _p(qsl), _p(seq_lens), None, 0, 0, None, n, hq, d, 0, 1, 0, 0, 1.0 / math.log(logn_ref), None,
+              _stream(q))
+    return qs
+
+
 def merge(out_l, lse_l, out_f, lse_f, out, qsl, seq_lens, *, window, block, alpha):
     """Writes the mass-weighted merge into out [n, Hq, D] (fold/kernels.py:135-142).
 

@@ -80,7 +80,9 @@ int fold_far_query(const void* q, int64_t q_stride_tok, int64_t q_stride_head, v
 
 /* ReRoPE query pair. Replaces rerope_queries / _rerope_query_kernel (fold/kernels.py:49-83,
  * 122-132): qs = q * max(1, log(H + t + 1) * inv_log_ref) when inv_log_ref > 0, else q;
- * qf = qs rotated by (D - H) (minus t when `constant`). Writes far_len[0] (may be NULL). */
+ * qf = qs rotated by (D - H) (minus t when `constant`). Writes far_len[0] (may be NULL).
+ * With qf and rope_table both NULL only qs is written: the ReRoPE query scale of the sliding and
+ * native-window layers, replacing logn_scale_rows (fold/attention.py:76-83). */
 int fold_rerope_query(const void* q, int64_t q_stride_tok, int64_t q_stride_head, void* qs, int64_t qs_stride_tok,
                       int64_t qs_stride_head, void* qf, int64_t qf_stride_tok, int64_t qf_stride_head,
                       const int* qsl, const int* seq_lens, const float* rope_table, int table_rows, int rot_dim,
@@ -203,7 +205,9 @@ int fold_combine(const float* o_part, const float* lse_part, int splits, float* 
  * attention plugin only the step's tensors, a C runtime without a caching allocator). No
  * counterpart in the reference. The same work as fold_far_read followed by fold_merge, with the
  * split partials kept in a 16 MiB static device array of the library (4 Mi floats per GPU, held
- * from library load to process exit) instead of caller memory: requests needing more than
+ * on each device from the library's first use there, typically the first kernel call, until
+ * process exit; CUDA_MODULE_LOADING=EAGER moves it to context creation) instead of caller
+ * memory: requests needing more than
  * splits * n * hq * (hd + 1) = 4194304 floats fail with FOLD_ERR_INVALID_ARGUMENT. The first call
  * on each device looks the array up (cudaGetSymbolAddress); make it before any stream capture.
  * The array is shared by every call on a device and keeps the last call's partials (each call

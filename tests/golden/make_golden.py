@@ -2,7 +2,8 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of the reference>
+    (or FOLD_REFERENCE=<checkout> python tests/golden/make_golden.py)
 
 What it runs, all on the CPU:
   * fold.reference.fold_block (fold/reference.py:21-53) on seeded inputs;
@@ -10,7 +11,10 @@ What it runs, all on the CPU:
     CPU interpreter (TRITON_INTERPRET=1), i.e. the reference's own kernels;
   * the side-cache scatter of fold.attention._wrap_context_kv (fold/attention.py:233-265) with
     a stand-in drafter object whose projections return fixed tensors and whose vLLM rotary op
-    is a no-op (the side cache stores keys before RoPE, fold/attention.py:240).
+    is a no-op (the side cache stores keys before RoPE, fold/attention.py:240);
+  * the plugin surface: fold.attention.install, use_full_draft_storage and FoldWorkspace
+    (fold/attention.py:44-73,270-375) and fold.rope.drafter_rope (fold/rope.py:14-28) on the
+    stand-in drafters of tests/standins.py, recording each report or error (plugin_surface.json).
 
 Inputs come from numpy's default_rng so that they regenerate bit for bit on any machine; each
 file stores the inputs it needs (small cases) or their sha256 (the full config-1 case).
@@ -245,21 +249,82 @@ def gen_append(torch, attention):
     print("append pages", ws[0].side_pages)
 
 
+def _outcome(fn):
+    """{"value": fn()} or {"error": exception class name, "message": its text}."""
+    try:
+        return {"value": fn()}
+    except Exception as e:  # noqa: BLE001 - the error itself is the recorded outcome
+        return {"error": type(e).__name__, "message": str(e)}
+
+
+def gen_plugin_surface(torch, attention, rope):
+    """The reference's install / use_full_draft_storage / FoldWorkspace / drafter_rope on the
+    stand-in drafters of tests/standins.py: every report, every layer's wrapper and workspace
+    geometry, every error."""
+    import json
+
+    sys.path.insert(0, str(HERE.parents[1]))
+    from tests import standins as si
+
+    out = {}
+    for name, (scn, kwargs) in si.INSTALL_SCENARIOS.items():
+        def run(scn=scn, kwargs=kwargs):
+            spec = si.build_speculator(scn)
+            rep = attention.install(spec, **kwargs)
+            again = attention.install(spec, **kwargs)
+            got = si.report_of(spec, rep)
+            got["idempotent"] = again is rep
+            return got
+        out[name] = _outcome(run)
+    for name, scn in si.STORAGE_SCENARIOS.items():
+        def run(scn=scn):
+            spec = si.build_speculator(scn)
+            res = attention.use_full_draft_storage(spec)
+            again = attention.use_full_draft_storage(spec)
+            ctx = spec.vllm_config.compilation_config.static_forward_context
+            return {"result": dict(res), "idempotent": again is res,
+                    "specs": {k: layer.get_kv_cache_spec("cfg") for k, layer in ctx.items()}}
+        out[name] = _outcome(run)
+    for name, kwargs in si.ROPE_SCENARIOS.items():
+        def run(kwargs=kwargs):
+            r = rope.drafter_rope(si.make_rotary(**kwargs))
+            return {"inv_freq": [float(x) for x in r.inv_freq.tolist()], "rotary_dim": r.rotary_dim,
+                    "head_dim": r.head_dim, "dtype": str(r.inv_freq.dtype)}
+        out[name] = _outcome(run)
+    for name, (w, b, max_len, mode, shape) in si.WORKSPACE_SCENARIOS.items():
+        def run(w=w, b=b, max_len=max_len, mode=mode, shape=shape):
+            ws = attention.FoldWorkspace(torch.zeros(shape, dtype=torch.bfloat16), w, b, max_len,
+                                         inv_freq=torch.ones(shape[-1] // 4 if len(shape) == 4 else 1),
+                                         far_distance=0, mode=mode)
+            return {"side_shape": list(ws.side.shape), "side_pages": ws.side_pages, "far_distance": ws.far_distance,
+                    "local_splits": ws.local_splits, "window": ws.window, "block": ws.block}
+        out[name] = _outcome(run)
+    (HERE / "plugin_surface.json").write_text(json.dumps(out, indent=1, sort_keys=True) + "\n")
+    print("plugin surface cases", len(out))
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--reference", default=os.environ.get("FOLD_REFERENCE", "/root/reference"))
+    p.add_argument("--reference", default=os.environ.get("FOLD_REFERENCE"),
+                   help="checkout of the reference (or set FOLD_REFERENCE)")
     p.add_argument("--no-full", action="store_true", help="skip the config-1 case (about 10 s)")
+    p.add_argument("--only", choices=["plugin"], help="regenerate only one group of vectors")
     args = p.parse_args()
+    if not args.reference:
+        p.error("give --reference <checkout> or set FOLD_REFERENCE")
     sys.path.insert(0, args.reference)
     import torch
     from fold import attention, kernels
     from fold import reference as ref
+    from fold import rope
 
     torch.set_num_threads(os.cpu_count() or 1)
-    gen_fold_block(torch, ref, not args.no_full)
-    gen_queries(torch, kernels)
-    gen_merge(torch, kernels)
-    gen_append(torch, attention)
+    if args.only != "plugin":
+        gen_fold_block(torch, ref, not args.no_full)
+        gen_queries(torch, kernels)
+        gen_merge(torch, kernels)
+        gen_append(torch, attention)
+    gen_plugin_surface(torch, attention, rope)
 
 
 if __name__ == "__main__":

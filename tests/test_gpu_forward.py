@@ -154,3 +154,90 @@ def test_native_window_layer_matches_oracle():
     want, _ = fo.window_read(q_roped, k_roped, fo.bf16_round(np.concatenate((vc, vb))), t, native, 0, True,
                              g["scale"])
     assert np.abs(out.float().cpu().numpy().reshape(want.shape) - want).max() <= OUT_ATOL
+
+
+# ---------------------------------------------------------------- ReRoPE mode (fold-mode=rerope)
+RE_CASE = "fold_block_regen_qwen3_like.npz"  # t = 3000: the log-n scale is above 1 for ref 256
+LOGN_REF = 256
+
+
+def rerope_inputs(g):
+    q, kc, vc, kb, vb = g["q"], g["k_ctx"], g["v_ctx"], g["k_blk"], g["v_blk"]
+    t, B = kc.shape[0], q.shape[0]
+    f = g["inv_freq"]
+    keys = np.concatenate((kc, kb)).astype(np.float64)
+    vals = np.concatenate((vc, vb)).astype(np.float64)
+    k_roped = fo.bf16_round(fo.rotate(keys, np.arange(t + B), f))
+    q_roped = fo.bf16_round(fo.rotate(q, np.arange(t, t + B), f))
+    return t, B, f, keys, vals, k_roped, q_roped
+
+
+def test_logn_scale_rows_kernel_matches_oracle():
+    """logn_scale_rows (fold/attention.py:76-83) as the query-scale path of the rerope kernel."""
+    from fold_b200.attention import logn_scale_rows
+    rng = np.random.default_rng(12)
+    n, hq, hd = 10, 8, 128
+    for hist in (0, 100, 5000, 131062):
+        q = bf16_tensor(rng.standard_normal((n, hq, hd), dtype=np.float32))
+        qsl = torch.tensor([0, n], dtype=torch.int32, device="cuda")
+        seq = torch.tensor([hist + n], dtype=torch.int32, device="cuda")
+        got = logn_scale_rows(q, qsl, seq, 4096).float().cpu().numpy()
+        want = fo.logn_scale_rows(q.float().cpu().numpy(), hist, 4096)
+        assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max()
+        assert (got == fo.bf16_round(want)).mean() > 0.98
+
+
+def test_fold_forward_rerope_mode_matches_oracle():
+    """FoldAttention in rerope mode (fold/attention.py:158-160): the window read of the log-n
+    scaled query, the far read of that query rotated to the constant distance D."""
+    g = golden_block_case(RE_CASE)
+    ws, original, meta, query, kv_cache, output = build_step(g)
+    ws.mode, ws.logn_ref = "rerope", LOGN_REF
+    out = FoldAttention(original, ws).forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    ws.check()
+    t, B, f, keys, vals, k_roped, q_roped = rerope_inputs(g)
+    W, alpha, scale = g["window"], g["alpha"], g["scale"]
+    qs, qf = fo.rerope_queries(q_roped, t, f, W + B, LOGN_REF)
+    o_l, lse_l = fo.local_read(fo.bf16_round(qs), k_roped, fo.bf16_round(vals), t, W, B, scale)
+    lim = fo.far_row_limits(t, W, B, B)
+    o_f, lse_f = fo.far_read(fo.bf16_round(qf), fo.bf16_round(keys[:t]), fo.bf16_round(vals[:t]), lim, scale * alpha)
+    want = fo.merge(o_l, lse_l, o_f, lse_f, t, W, B, alpha)
+    assert np.abs(out.float().cpu().numpy().reshape(want.shape) - want).max() <= OUT_ATOL
+
+
+def test_sliding_fold_forward_rerope_mode_matches_oracle():
+    """SlidingFoldAttention in rerope mode (fold/attention.py:203-207): the native causal read of
+    the log-n scaled query, the far read of that query rotated to the constant distance."""
+    g = golden_block_case(RE_CASE)
+    ws, original, meta, query, kv_cache, output = build_step(g, sliding=True)
+    ws.mode, ws.logn_ref = "rerope", LOGN_REF
+    out = SlidingFoldAttention(original, ws).forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    ws.check()
+    t, B, f, keys, vals, k_roped, q_roped = rerope_inputs(g)
+    W, alpha, scale = g["window"], g["alpha"], g["scale"]
+    qn = fo.bf16_round(fo.logn_scale_rows(q_roped, t, LOGN_REF))
+    _, qf = fo.rerope_queries(qn, t, f, W + B, 0)
+    o_l, lse_l = fo.window_read(qn, k_roped, fo.bf16_round(vals), t, W + B - 1, 0, True, scale)
+    lim = fo.far_row_limits(t, W, B, B)
+    o_f, lse_f = fo.far_read(fo.bf16_round(qf), fo.bf16_round(keys[:t]), fo.bf16_round(vals[:t]), lim, scale * alpha)
+    want = fo.merge(o_l, lse_l, o_f, lse_f, t, W, B, alpha)
+    assert np.abs(out.float().cpu().numpy().reshape(want.shape) - want).max() <= OUT_ATOL
+
+
+def test_native_window_layer_with_logn_scale_matches_oracle():
+    """NativeWindowAttention with logn_ref (fold/attention.py:113-115)."""
+    from fold_b200.attention import NativeWindowAttention
+    g = golden_block_case(RE_CASE)
+    ws, original, meta, query, kv_cache, output = build_step(g)
+    native = 300
+    original.sliding_window = (native, 0)
+    layer = NativeWindowAttention(original, LOGN_REF, block=query.shape[0], device=query.device)
+    out = layer.forward(None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    layer.check()
+    t, B, f, keys, vals, k_roped, q_roped = rerope_inputs(g)
+    qn = fo.bf16_round(fo.logn_scale_rows(q_roped, t, LOGN_REF))
+    want, _ = fo.window_read(qn, k_roped, fo.bf16_round(vals), t, native, 0, True, g["scale"])
+    assert np.abs(out.float().cpu().numpy().reshape(want.shape) - want).max() <= OUT_ATOL

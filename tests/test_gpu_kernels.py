@@ -1,7 +1,10 @@
 """Parity of the CUDA kernels with the CPU oracle, called through the C-ABI (fold_b200.kernels).
 
 append/gather: bit-exact. far query: within one bf16 ulp of the oracle's table rotation.
-far read + merge: output max-abs 2e-2 against the float64 oracle, LSE within 1e-3 relative.
+far read + merge: output max-abs 2e-2 against the float64 oracle (absolute, on every channel,
+the x8 outlier channels included), LSE within 1e-3 relative. The full-length cases of the three
+long-context shapes (129,024 far keys at head_dim 128; 258,048 at head_dim 256 with 64 and 16
+query rows per KV head) print their measured max-abs error.
 """
 import numpy as np
 import pytest
@@ -148,16 +151,61 @@ def run_far(n, hq, hkv, hd, far_keys, *, splits, window=64, extra=0, outliers=0,
     lim = np.minimum(lim, pos_lo + held)
     kf, vf = kb[local], vb[local]
     o_w, lse_w = fo.far_read(to64(qf), kf, vf, lim, scale, key_lo=pos_lo)
-    # per (query head, channel) value scale: the bar is 2e-2 in units of the channel's scale
-    # (x8 outlier channels of V carry x8 the bf16 rounding of P)
-    vscale = np.maximum(np.repeat(vf.std(axis=0), hq // hkv, axis=0), 1.0) if vf.shape[0] > 1 else np.ones((hq, hd))
-    return to64(o_d), to64(lse_d), o_w, lse_w, dict(o_part=o_part, lse_part=lse_part, qf=qf, q=q, hist=hist,
-                                                    vscale=vscale)
+    return to64(o_d), to64(lse_d), o_w, lse_w, dict(o_part=o_part, lse_part=lse_part, qf=qf, q=q, hist=hist)
 
 
-def out_close(o_d, o_w, vscale):
-    err = np.abs(o_d - o_w) / vscale[None]
-    assert err.max() <= OUT_ATOL, f"max scaled error {err.max()}"
+def out_close(o_d, o_w, what=""):
+    """The output bar: max-abs 2e-2, absolute, over every channel (outlier channels included)."""
+    err = float(np.abs(o_d - o_w).max())
+    print(f"{what} output max-abs error {err:.5f} (bar {OUT_ATOL})")
+    assert err <= OUT_ATOL, f"max error {err}"
+
+
+def run_far_device(n, hq, hkv, hd, far_keys, *, splits, window, seed, outliers=0, theta=1e6):
+    """Far read of a full-length side cache generated on the device (seeded torch generator), the
+    oracle computed per KV head from the same bf16 keys and values. Returns (device o, lse,
+    oracle o, lse)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    L = far_keys
+    k = torch.randn((L, hkv, hd), device="cuda", generator=gen).to(torch.bfloat16)
+    v = torch.randn((L, hkv, hd), device="cuda", generator=gen).to(torch.bfloat16)
+    if outliers:
+        ch = torch.randperm(hd, generator=torch.Generator().manual_seed(seed))[:outliers].cuda()
+        k[..., ch] *= 8
+        v[..., ch] *= 8
+    pages = -(-L // 256) + 1
+    side = torch.zeros((pages, hkv, 256, 2 * hd), device="cuda", dtype=torch.bfloat16)
+    full = L // 256
+    side[:full] = torch.cat((k[:full * 256], v[:full * 256]), -1).view(full, 256, hkv, 2 * hd).transpose(1, 2)
+    if L > full * 256:
+        side[full, :, :L - full * 256] = torch.cat((k[full * 256:], v[full * 256:]), -1).transpose(0, 1)
+    q = torch.randn((n, hq, hd), device="cuda", generator=gen).to(torch.bfloat16)
+    B = n
+    hist = far_keys + window  # far_len = hist - W - B + n = far_keys
+    f = fo.inv_freq(theta, hd)
+    table = rope_table(torch.from_numpy(f).cuda(), hist + 2 * window + 2 * B + 1, "cuda")
+    qsl, seq = lengths(n, hist)
+    o_part = torch.empty((splits, n, hq, hd), device="cuda", dtype=torch.float32)
+    lse_part = torch.empty((splits, hq, n), device="cuda", dtype=torch.float32)
+    far_len = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qf = torch.empty_like(q)
+    scale = hd ** -0.5 * 2.0
+    kernels.far_read(q, qsl, seq, side, o_part, lse_part, window=window, block=B, far_distance=window + B,
+                     softmax_scale=scale, table=table, far_len=far_len, qf=qf, capacity=L, err=err)
+    o_d, lse_d = kernels.combine(o_part, lse_part)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and int(far_len.item()) == far_keys
+    lim = fo.far_row_limits(hist, window, B, n)
+    g = hq // hkv
+    qf64 = to64(qf)
+    o_w, lse_w = np.zeros((n, hq, hd)), np.zeros((hq, n))
+    for h in range(hkv):  # one KV head at a time keeps the float64 copies at a few hundred MB
+        kh, vh = to64(k[:, h:h + 1]), to64(v[:, h:h + 1])
+        oh, lh = fo.far_read(qf64[:, h * g:(h + 1) * g], kh, vh, lim, scale)
+        o_w[:, h * g:(h + 1) * g], lse_w[h * g:(h + 1) * g] = oh, lh
+    return to64(o_d), to64(lse_d), o_w, lse_w
 
 
 FAR_CASES = [
@@ -192,7 +240,7 @@ def test_far_read_no_far_keys_gives_empty_rows(far_kernel):
 
 def test_far_read_outliers_partial_rotary(far_kernel):
     o_d, lse_d, o_w, lse_w, x = run_far(10, 32, 8, 128, 3000, splits=8, outliers=4, rot=64, extra=200)
-    out_close(o_d, o_w, x["vscale"])
+    out_close(o_d, o_w, f"{far_kernel} 3000 keys, x8 outliers, rotary 64:")
     lse_close(lse_d, lse_w)
 
 
@@ -206,7 +254,25 @@ def test_far_read_shard_of_cache(far_kernel):
 def test_far_read_full_context_llama_shape(far_kernel):
     """Llama-3.1-8B drafter shape at 131072 context (129024 far keys), outlier channels x8."""
     o_d, lse_d, o_w, lse_w, x = run_far(10, 32, 8, 128, 129024, splits=18, window=2048, outliers=4, seed=1)
-    out_close(o_d, o_w, x["vscale"])
+    out_close(o_d, o_w, f"{far_kernel} 128K Llama shape (129024 keys, x8 outliers):")
+    lse_close(lse_d, lse_w)
+
+
+@pytest.mark.parametrize("n,hq,hkv,splits", [(16, 16, 4, 37), (8, 16, 8, 18)])
+def test_far_read_full_context_hd256(n, hq, hkv, splits, far_kernel):
+    """The 262144-context head_dim-256 shapes: 258048 far keys; 16/4 heads with a 16-token block
+    (64 query rows per KV head) and 16/8 heads with an 8-token block (16 rows)."""
+    o_d, lse_d, o_w, lse_w = run_far_device(n, hq, hkv, 256, 258048, splits=splits, window=4096, seed=n + hkv)
+    out_close(o_d, o_w, f"{far_kernel} 262K hd 256, {hq}/{hkv} heads, block {n}:")
+    lse_close(lse_d, lse_w)
+
+
+def test_far_read_full_context_llama_shape_device_generated(far_kernel):
+    """The 128K Llama shape again with device-generated inputs and the x8 outlier channels on K
+    and V (a second seed)."""
+    o_d, lse_d, o_w, lse_w = run_far_device(10, 32, 8, 128, 129024, splits=18, window=2048, seed=7, outliers=4,
+                                            theta=5e5)
+    out_close(o_d, o_w, f"{far_kernel} 128K Llama shape (device inputs, x8 outliers):")
     lse_close(lse_d, lse_w)
 
 

@@ -37,17 +37,22 @@ def make_step(seed, n, hq, hkv, hd, far_keys, window):
                 window=window, scale=2.0 * hd ** -0.5, L=L)
 
 
-def static_call(s, splits):
-    out = torch.full((s["n"], s["hq"], s["hd"]), float("nan"), device="cuda", dtype=torch.bfloat16)
-    far_len = torch.zeros(1, dtype=torch.int32, device="cuda")
+def static_buffers(s):
+    """The caller's own buffers of a call: output, far_len and the device error word."""
+    return (torch.full((s["n"], s["hq"], s["hd"]), float("nan"), device="cuda", dtype=torch.bfloat16),
+            torch.zeros(1, dtype=torch.int32, device="cuda"), torch.zeros(1, dtype=torch.int32, device="cuda"))
+
+
+def static_call(s, splits, bufs=None):
+    out, far_len, err = bufs or static_buffers(s)
     q, o_l, lse_l, table, side = s["q"], s["o_l"], s["lse_l"], s["table"], s["side"]
     _lib.call("fold_far_read_merge_static", q.data_ptr(), q.stride(0), q.stride(1), s["qsl"].data_ptr(),
               s["seq"].data_ptr(), table.data_ptr(), table.shape[0], table.shape[1], side.data_ptr(), side.shape[0],
               0, s["L"], far_len.data_ptr(), o_l.data_ptr(), o_l.stride(0), o_l.stride(1), lse_l.data_ptr(),
               lse_l.stride(0), lse_l.stride(1), out.data_ptr(), out.stride(0), out.stride(1), splits, s["n"], s["hq"],
-              s["hkv"], s["hd"], s["window"], s["n"], s["window"] + s["n"], s["scale"], 0.5, None,
+              s["hkv"], s["hd"], s["window"], s["n"], s["window"] + s["n"], s["scale"], 0.5, err.data_ptr(),
               torch.cuda.current_stream().cuda_stream)
-    return out, far_len
+    return out, far_len, err
 
 
 def regular_call(s, splits):
@@ -68,12 +73,32 @@ def test_static_scratch_matches_regular_path_on_two_calls():
     first = make_step(1, 10, 32, 8, 128, 20000, 2048)
     second = make_step(2, 8, 16, 8, 256, 3000, 512)
     for s, splits in ((first, 18), (second, 5)):
-        got, far_len = static_call(s, splits)
+        got, far_len, err = static_call(s, splits)
         want = regular_call(s, splits)
         torch.cuda.synchronize()
+        assert int(err.item()) == 0, "the static path recorded a device error"
         assert int(far_len.item()) == s["L"] - s["n"] - s["window"]
         assert torch.isfinite(got.float()).all()
         assert (got.float() - want.float()).abs().max().item() <= OUT_ATOL
+
+
+def test_static_call_allocates_no_device_memory():
+    """The property the entry point exists for: once the library is loaded on the device, a call
+    changes neither the device's free memory nor the torch allocator's counters."""
+    s = make_step(4, 10, 32, 8, 128, 20000, 2048)
+    static_call(s, 18)  # first use on the device: loads the library's module (and its static array)
+    bufs = static_buffers(s)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    stats0 = torch.cuda.memory_stats()
+    static_call(s, 18, bufs)
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    stats1 = torch.cuda.memory_stats()
+    assert int(bufs[2].item()) == 0
+    assert free1 == free0, f"device free memory moved by {free0 - free1} bytes"
+    for key in ("allocation.all.allocated", "segment.all.allocated", "reserved_bytes.all.allocated"):
+        assert stats1.get(key, 0) == stats0.get(key, 0), key
 
 
 def test_static_scratch_rejects_oversize_requests():
