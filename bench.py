@@ -34,6 +34,8 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -287,7 +289,12 @@ def run_gpu(args):
     # --fused: the far read ends with the exchange (of one rank at N = 1) and the merge in one cooperative
     # launch; otherwise the far read and the merge (or the peer exchange kernel) are two launches
     fused = args.exchange == "p2p" and args.fused
-    peer = PeerExchange(n=B, hq=hq, hd=hd, device=dev) if args.exchange == "p2p" and (world > 1 or fused) else None
+    # at N > 1 both data planes are built: the step runs the chosen one, the other is timed beside it
+    peer = PeerExchange(n=B, hq=hq, hd=hd, device=dev) if world > 1 or fused else None
+    comm = 0
+    if world > 1:
+        dist.barrier(device_ids=[local])  # the NCCL communicator exists from here on
+        comm = int(dist.group.WORLD._get_backend(dev)._comm_ptr())
 
     def far(i):
         kernels.far_read(q_all[i], qsl, seq_all[i: i + 1], side, o_part, lse_part, window=W, block=B,
@@ -299,7 +306,7 @@ def run_gpu(args):
             kernels.append(new_k[i - 1, :a], new_v[i - 1, :a], new_pos[i - 1, :a], new_pos[i - 1, :a], side,
                            pos_lo=pos_lo, skip_foreign=world > 1, err=err)
 
-    def step(i):
+    def step(i, exchange=args.exchange):
         append(i)
         seq = seq_all[i: i + 1]
         if fused:
@@ -308,15 +315,13 @@ def run_gpu(args):
                                       table=table, pos_lo=pos_lo, capacity=length, err=err)
             return
         far(i)
-        if peer is not None:
-            peer.merge(o_part, lse_part, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=ALPHA, err=err)
-        elif world > 1:
-            kernels.combine(o_part, lse_part, o_mine, lse_mine)
-            dist.all_gather_into_tensor(recv, send)
-            o_all, lse_all = unpack_partials(recv, world, B, hq, hd)
-            kernels.merge(o_l, lse_l, o_all, lse_all, out, qsl, seq, window=W, block=B, alpha=ALPHA)
-        else:
+        if world == 1:
             kernels.merge(o_l, lse_l, o_part, lse_part, out, qsl, seq, window=W, block=B, alpha=ALPHA)
+        elif exchange == "p2p":
+            peer.merge(o_part, lse_part, o_l, lse_l, out, qsl, seq, window=W, block=B, alpha=ALPHA, err=err)
+        else:  # combine + ncclAllGather (fold_allgather_partials), then the merge of the world's partials
+            o_all, lse_all = kernels.allgather_partials(comm, o_part, lse_part, send, recv)
+            kernels.merge(o_l, lse_l, o_all, lse_all, out, qsl, seq, window=W, block=B, alpha=ALPHA)
 
     def barrier():
         if world > 1:
@@ -412,15 +417,39 @@ def run_gpu(args):
         torch.cuda.synchronize()
         fused_ms = f0.elapsed_time(f1) / args.steps
         del fg
+    # N > 1: the same steps with the other data plane (peer exchange or NCCL all-gather), timed
+    # the same way (graph of K steps after the same untimed passes, barrier, max over ranks)
+    alt, alt_ms = None, 0.0
+    if world > 1 and not fused:
+        alt = "nccl" if args.exchange == "p2p" else "p2p"
+        for j in range(args.warmup):
+            step(j, alt)
+        torch.cuda.synchronize()
+        alt_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(alt_graph):
+            for j in range(args.steps):
+                step(args.warmup + j, alt)
+        alt_graph.replay()
+        for _ in range(pre):
+            alt_graph.replay()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        f0.record(stream)
+        alt_graph.replay()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        alt_ms = f0.elapsed_time(f1)
+        del alt_graph
     window = run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err,
                         append) if world == 1 else None
     # every rank takes part in the reduction before any rank may raise (same collectives everywhere)
-    t = torch.tensor([ms, far_ms, far_sustained_ms, float(err.item())], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms, far_ms, far_sustained_ms, float(err.item()), alt_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, far_ms, far_sustained_ms = float(t[0]), float(t[1]), float(t[2])
+    ms, far_ms, far_sustained_ms, alt_ms = float(t[0]), float(t[1]), float(t[2]), float(t[4])
     if int(t[3]):
-        raise RuntimeError(f"device error word {int(t[2])} on some rank")
+        raise RuntimeError(f"device error word {int(t[3])} on some rank")
     us_step = 1000.0 * ms / args.steps
 
     # algorithmic bytes of one far-read launch on this rank: its K/V rows + q + partials
@@ -429,7 +458,10 @@ def run_gpu(args):
     part_bytes = splits * (B * hq * hd + hq * B) * 4
     alg = kv_bytes + B * hq * hd * 2 + part_bytes
     hbm_peak, peak_kind = peaks()
-    achieved = alg / (far_ms * 1e-3) / 1e9
+    # the far read as it runs inside the step: K launches back to back after 0.3 s of load, when
+    # the board sits at its power cap (the burst figure is kept beside it)
+    achieved = alg / (far_sustained_ms * 1e-3) / 1e9
+    achieved_burst = alg / (far_ms * 1e-3) / 1e9
     traffic = profile_traffic(args.config) if world == 1 else None
 
     e2e = None
@@ -458,26 +490,37 @@ def run_gpu(args):
                                         and world == 1 else "append + far read ending with the peer exchange and the "
                                         "merge in one cooperative kernel" if fused else "append + far read + merge"
                                         if world == 1 else "append + far read + peer exchange kernel"
-                                        if peer is not None else "append + far read + combine + NCCL all-gather + "
-                                        "merge"),
+                                        if args.exchange == "p2p" else "append + far read + combine and "
+                                        "ncclAllGather (fold_allgather_partials) + merge"),
                        "exchange": None if world == 1 else (
                            "peer-to-peer (NVLink stores of self-validating lines, combine and merge fused)"
-                           if peer is not None else "NCCL all-gather"),
+                           if args.exchange == "p2p" else "NCCL all-gather"),
                        "timing": "eager launches" if args.eager else "CUDA graph of the K timed steps",
                        "l2": "inputs larger than L2 (side cache %.0f MB per GPU)" % (side.numel() * 2 / 1e6)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-                         "kernel": "far_read_kernel", "kernel_us": round(far_ms * 1000, 3),
-                         "kernel_timing": "burst: the far read alone, one graph of K launches after idle",
+                         "kernel": "far_read_kernel", "kernel_us": round(far_sustained_ms * 1000, 3),
+                         "kernel_timing": "sustained: the far read alone, one graph of K launches timed after 0.3 s "
+                                          "of back-to-back replays (the power-capped clock of the step)",
                          "kernel_us_sustained": round(far_sustained_ms * 1000, 3),
+                         "kernel_us_burst": round(far_ms * 1000, 3),
+                         "achieved_burst": round(achieved_burst, 1),
+                         "frac_burst": round(achieved_burst / hbm_peak, 4),
                          "fused_kernel_us": None if fused_ms is None else round(fused_ms * 1000, 3),
                          "algorithmic_bytes": int(alg), "traffic": traffic},
-            "gpu_launches": args.steps * (2 if fused else 3 if world == 1 or peer is not None else 4),
+            "gpu_launches": args.steps * (2 if fused else 3 if world == 1 or args.exchange == "p2p" else 5),
             "clocks": clocks.summary(),
             "e2e": e2e,
         }
         if window is not None:
             line["window_read"] = window
+        if alt is not None:
+            line["exchange_alternative"] = {
+                "exchange": alt, "us_per_step": round(1000.0 * alt_ms / args.steps, 3),
+                "how": ("append + far read + combine and ncclAllGather of the per-rank partials "
+                        "(fold_allgather_partials) + merge" if alt == "nccl" else
+                        "append + far read + peer exchange kernel"),
+                "timing": "the same K steps as one CUDA graph, same untimed passes, max over ranks"}
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, args.seed)
         print(json.dumps(line), flush=True)
@@ -708,75 +751,183 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
             step(i, last)
         compute.wait_stream(down)
 
-    run(0, args.warmup)
-    torch.cuda.synchronize()
-    # untimed passes over the timed steps first, so that the timed region runs under the same
-    # sustained load (and power-capped clock) as the device-timed step; the count is rank 0's
-    t0 = time.perf_counter()
-    run(args.warmup, total)
-    torch.cuda.synchronize()
-    pre = torch.tensor([max(0, min(20, int(0.3 / max(time.perf_counter() - t0, 1e-4))))], device=dev)
-    if world > 1:
-        dist.broadcast(pre, src=0)
-    for _ in range(int(pre.item())):
-        run(args.warmup, total)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier(device_ids=[local])
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(compute)
-    run(args.warmup, total)
-    e1.record(compute)
-    torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    done = torch.cuda.Event()
+
+    def run_serial(first, last):
+        """One step after the other as a drafter must take them (step i + 1's query depends on
+        step i's output): upload, replay, read back, wait for the output on the host."""
+        sl = slots[0]
+        for i in range(first, last):
+            sl.d_in.copy_(h_in[i], non_blocking=True)
+            sl.graph.replay()
+            h_out[0].copy_(sl.out, non_blocking=True)
+            done.record(compute)
+            done.synchronize()
+
+    def timed(fn):
+        """fn(warmup + ...) steps timed with events on the compute stream after untimed passes
+        (the same sustained load and power-capped clock as the device-timed step; rank 0's pass
+        count), max over ranks."""
+        fn(0, args.warmup)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fn(args.warmup, total)
+        torch.cuda.synchronize()
+        pre = torch.tensor([max(0, min(20, int(0.3 / max(time.perf_counter() - t0, 1e-4))))], device=dev)
+        if world > 1:
+            dist.broadcast(pre, src=0)
+        for _ in range(int(pre.item())):
+            fn(args.warmup, total)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(compute)
+        fn(args.warmup, total)
+        e1.record(compute)
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return 1000.0 * float(ms) / args.steps
+
+    us_serial = timed(run_serial)
+    us_pipelined = timed(run)
     for sl in slots:
         sl.graph = None  # graphs that hold collectives go before the process group
     torch.cuda.synchronize()
     if sharded is not None and sharded.peer is not None and sharded.peer is not peer:
         sharded.peer.close()
-    return {"value": round(1000.0 * float(ms) / args.steps, 3), "unit": "us/draft-step",
+    api = ("FoldWorkspace.append + " + (
+        "PeerExchange.read_merge (far read + merge in one cooperative kernel)" if peer is not None and
+        sharded is None else "ShardedFarMemory.step_merge (far read + peer exchange + merge in one "
+        "cooperative kernel)" if peer is not None else "ShardedFarMemory step/merge" if sharded is not None
+        else "FoldWorkspace.read_far + kernels.merge") + " (fold_b200 C-ABI), captured once per input buffer in a "
+        "CUDA graph and replayed per step")
+    return {"value": round(us_serial, 3), "unit": "us/draft-step",
             "h2d_bytes_per_step": rec, "d2h_bytes_per_step": B * hq * hd * 2,
-            "api": ("FoldWorkspace.append + " + (
-                "PeerExchange.read_merge (far read + merge in one cooperative kernel)" if peer is not None and
-                sharded is None else "ShardedFarMemory.step_merge (far read + peer exchange + merge in one "
-                "cooperative kernel)" if peer is not None else "ShardedFarMemory step/merge" if sharded is not None
-                else "FoldWorkspace.read_far + kernels.merge") + " (fold_b200 C-ABI), captured "
-                    "once per input buffer in a CUDA graph and replayed per step; per step one pinned host->device "
-                    "copy of the step's inputs and one device->host copy of its output, each on its own stream, "
-                    "double-buffered so that they overlap the neighbouring steps")}
+            "api": api + "; per step, serially: one pinned host->device copy of the step's inputs, the replay, one "
+                         "device->host copy of its output, and a host wait for that output before the next step",
+            "pipelined": {"value": round(us_pipelined, 3), "unit": "us/draft-step",
+                          "how": "the same steps with the copies on their own streams, double-buffered so that "
+                                 "step i + 1's upload and step i - 1's read-back overlap step i (throughput of "
+                                 "independent steps, not a draft-step latency)"}}
 
 
 # ------------------------------------------------------------------------------ reference arm
+def port_step_heads(cfg, H, q, k, v, o_l, lse_l, inv_freq, kv_heads):
+    """The oracle port's far query + far read + merge of one step, restricted to the given KV
+    heads and their query heads (query heads are independent)."""
+    G = cfg["hq"] // cfg["hkv"]
+    qh = np.concatenate([np.arange(h * G, (h + 1) * G) for h in kv_heads])
+    sub = dict(cfg, hq=len(qh), hkv=len(kv_heads))
+    return cpu_step_oracle(sub, H, q[:, qh], k[:, kv_heads], v[:, kv_heads], o_l[:, qh], lse_l[qh], inv_freq)
+
+
+def reference_module():
+    """fold.reference of the reference package installed under baseline/_ref, or the import error."""
+    path = ROOT / "baseline" / "_ref"
+    if not (path / "fold" / "reference.py").exists():
+        return None, "the reference is not installed under baseline/_ref"
+    sys.path.insert(0, str(path))
+    try:
+        from fold import reference as ref  # noqa: PLC0415
+        return ref, None
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        return None, f"import of fold.reference failed: {type(e).__name__}: {e}"
+
+
+def time_fold_block(cfg, H, steps, warm, seed, budget_s=120.0):
+    """The reference's own CPU implementation, fold.reference.fold_block (fold/reference.py:21-53),
+    timed head-sliced: each step runs the whole draft block for one query head with its KV head
+    (GQA expanded, as fold_block requires; heads are independent), and the figure is scaled to all
+    query heads. Steps are the arm's own; if they do not fit the budget, every k-th is timed."""
+    import torch
+
+    ref, why = reference_module()
+    if ref is None:
+        return {"unavailable": why}
+    hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
+    G = hq // hkv
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(seed + 11)
+    L = int(H.max())
+    k_all = torch.randn((L, hkv, hd), generator=gen)
+    v_all = torch.randn((L, hkv, hd), generator=gen)
+    q_all = torch.randn((B, hq, hd), generator=gen)
+    kb, vb = torch.randn((B, hkv, hd), generator=gen), torch.randn((B, hkv, hd), generator=gen)
+    inv = torch.from_numpy((1.0 / (cfg["theta"] ** (np.arange(0, hd, 2) / hd))).astype(np.float32))
+
+    def one(i):
+        h = i % hq
+        kv = h // G
+        t = int(H[i])
+        return ref.fold_block(q_all[:, h:h + 1], k_all[:t, kv:kv + 1], v_all[:t, kv:kv + 1], kb[:, kv:kv + 1],
+                              vb[:, kv:kv + 1], window=W, alpha=ALPHA, inv_freq=inv, scale=hd ** -0.5)
+
+    t0 = time.perf_counter()
+    one(0)
+    first = time.perf_counter() - t0
+    every = max(1, int(np.ceil((steps + warm) * first / budget_s)))
+    times = []
+    for i in range(warm + steps):
+        if i % every:
+            continue
+        t0 = time.perf_counter()
+        one(i)
+        if i >= warm:
+            times.append(time.perf_counter() - t0)
+    if not times:
+        return {"unavailable": "no timed step fitted the budget"}
+    out = {"value": round(1e6 * float(np.mean(times)) * hq, 1), "unit": "us/draft-step", "kind": "reference",
+           "cores": torch.get_num_threads(),
+           "sample": f"fold.reference.fold_block (baseline/_ref, unmodified) on one of the {hq} query heads per "
+                     f"step (GQA expanded), {len(times)} timed steps of the {cfg['name']} workload"
+                     + (f" (every {every}th step of the arm's {steps})" if every > 1 else "")
+                     + f", scaled by {hq} heads; float64 inside, as the reference computes"}
+    torch.set_num_threads(1)
+    t0 = time.perf_counter()
+    one(warm)
+    out["value_1_thread"] = round(1e6 * (time.perf_counter() - t0) * hq, 1)
+    torch.set_num_threads(os.cpu_count() or 1)
+    return out
+
+
 def run_reference(args):
-    """The CPU implementation of the path (the oracle port; the reference's own GPU path needs
-    vLLM 0.28 and FlashAttention, and its CPU code is fold/reference.py, restated by the oracle),
-    on all host threads, on this arm's workload and metric."""
+    """The reference arm: the CPU implementation of the path on all host threads, over the arm's
+    own steps and warm-up, on the GPU arm's workload and metric. `value` is the oracle port's far
+    query + far read + merge (the work the GPU arm's metric counts; each step samples KV heads
+    when the whole step would not fit the time budget, scaled to all heads). The reference's own
+    fold_block (the whole FOLD block, local read and key rotation included) is timed beside it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     cfg = CONFIGS[args.config]
-    import numpy as np
-
     from oracle import fold_oracle as fo
 
-    steps = max(1, min(args.steps, 10))
-    warm = max(0, min(args.warmup, 1))
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    hkv = cfg["hkv"]
     acc, H = plan_steps(cfg, steps + warm, args.seed)
     q, k, v, o_l, lse_l = cpu_inputs(cfg, args.seed, int(H.max()))
     f = fo.inv_freq(cfg["theta"], cfg["hd"])
-    for i in range(warm):
-        cpu_step_oracle(cfg, int(H[i]), q, k, v, o_l, lse_l, f)
+    t0 = time.perf_counter()
+    port_step_heads(cfg, int(H[0]), q, k, v, o_l, lse_l, f, [0])
+    per_head = time.perf_counter() - t0
+    budget = 120.0
+    kv_sample = int(max(1, min(hkv, budget / max((steps + warm) * per_head, 1e-9))))
     times = []
-    for i in range(warm, warm + steps):
+    for i in range(warm + steps):
+        heads = [(i * kv_sample + j) % hkv for j in range(kv_sample)]
         t0 = time.perf_counter()
-        cpu_step_oracle(cfg, int(H[i]), q, k, v, o_l, lse_l, f)
-        times.append(time.perf_counter() - t0)
-    us = 1e6 * float(np.mean(times))
+        port_step_heads(cfg, int(H[i]), q, k, v, o_l, lse_l, f, heads)
+        if i >= warm:
+            times.append(time.perf_counter() - t0)
+    us = 1e6 * float(np.mean(times)) * hkv / kv_sample
     cores = os.cpu_count() or 1
-    sample = (f"{steps} whole draft steps of the {cfg['name']} workload: float64 numpy port of "
-              f"fold/reference.py's far read + merge (BLAS on {cores} threads)")
+    sample = (f"{steps} draft steps of the {cfg['name']} workload after {warm} warm-up steps: float64 numpy port of "
+              f"fold/reference.py's far query + far read + merge (BLAS on {cores} threads), "
+              + ("all KV heads per step" if kv_sample == hkv else
+                 f"{kv_sample} of {hkv} KV heads per step (with their query heads), scaled to {hkv}"))
     line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/draft-step",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": warm,
             "ms_per_step": round(us / 1000, 3), "higher_is_better": False, "scaling": "strong",
@@ -786,7 +937,8 @@ def run_reference(args):
             "cpu_baseline": {"value": round(us, 1), "unit": "us/draft-step", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(us, 1), "unit": "us/draft-step", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "reference_fold_block": time_fold_block(cfg, H, steps, warm, args.seed)}
     print(json.dumps(line), flush=True)
 
 

@@ -35,6 +35,7 @@ SIGNATURES = {
     "fold_merge": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp,
                    _i64, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp],
     "fold_combine": [_vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp],
+    "fold_allgather_partials": [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _vp],
     "fold_window_read": [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i64, _i64, _i64, _vp, _i32, _i32, _i32,
                          _i32, _f32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
     "fold_step_read": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp,

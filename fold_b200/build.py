@@ -79,7 +79,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         raise RuntimeError(f"nvcc failed for {failed}")
     tmp = LIB.with_suffix(".so.tmp")
     link = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-cudart", "static",
-            *map(str, objs), "-o", str(tmp)]
+            *map(str, objs), "-ldl", "-o", str(tmp)]
     if verbose:
         print(" ".join(link), flush=True)
     r = subprocess.run(link, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)

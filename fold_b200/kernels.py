@@ -354,6 +354,28 @@ def combine(o_part, lse_part, o_out=None, lse_out=None):
     return o_out, lse_out
 
 
+def allgather_partials(comm, o_part, lse_part, send, recv):
+    """The NCCL step of the sharded far read (fold_allgather_partials): this rank's split partials
+    o_part [S, n, Hq, D] / lse_part [S, Hq, n] are combined into `send` (one record of n*Hq*D +
+    Hq*n floats: o then lse) and every rank's record is all-gathered into recv [world * record]
+    with ncclAllGather on the communicator `comm` (an ncclComm_t address). Returns the gathered
+    (o [world, n, Hq, D], lse [world, Hq, n]) views of recv, ready for merge()."""
+    _require_cuda(o_part, lse_part, send, recv)
+    s, n, hq, d = o_part.shape
+    _check_partials(o_part, lse_part, n, hq, d, "allgather_partials")
+    per = n * hq * d + hq * n
+    if send.dtype != torch.float32 or recv.dtype != torch.float32 or not send.is_contiguous() \
+            or not recv.is_contiguous() or send.numel() < per or recv.numel() % per or recv.numel() < per:
+        raise FoldError("allgather_partials: send holds one record and recv whole records (float32, contiguous)")
+    if not comm:
+        raise FoldError("allgather_partials: no NCCL communicator")
+    _lib.call("fold_allgather_partials", int(comm), _p(o_part), _p(lse_part), s, _p(send), _p(recv), n, hq, d,
+              _stream(o_part))
+    world = recv.numel() // per
+    b = recv.view(world, per)
+    return b[:, : n * hq * d].view(world, n, hq, d), b[:, n * hq * d:].view(world, hq, n)
+
+
 FAR_READ_KERNELS = {"auto": -1, "mma": 0, "tc": 1}
 
 

@@ -9,9 +9,10 @@ Two ways to combine the per-rank partials:
   splits, stores the result into every rank's receive buffer over NVLink (CUDA IPC mappings of
   one device region per rank), raises a flag per item, waits for the peers' flags and merges
   with the window read. No collective library call on the step.
-* "nccl": the combine kernel, one all-gather of the partials (NCCL over NVLink on GPUs; any
-  torch.distributed backend works, gloo in the CPU tests), then the merge kernel, which combines
-  any number of partials.
+* "nccl": the combine kernel and one ncclAllGather of the per-rank partials over NVLink, issued by
+  the library on the process group's own NCCL communicator (fold_allgather_partials), then the
+  merge kernel, which combines any number of partials. Under another torch.distributed backend
+  (gloo in the CPU tests) the all-gather is torch's.
 
 The reference runs on one GPU; this module has no counterpart there. The exchange is the only
 cross-rank step of the path: the append and the reads are rank-local.
@@ -244,6 +245,7 @@ class ShardedFarMemory:
         self.plan, self.ws, self.group, self.exchange = plan, workspace, group, exchange
         self.peer = peer
         self._bufs = {}
+        self._comm_ptr = None
 
     def _buffers(self, n, hq, d, device):
         key = (n, hq, d)
@@ -259,6 +261,18 @@ class ShardedFarMemory:
     def append(self, k, v, positions, slots):
         self.ws.append(k, v, positions, slots)
 
+    def nccl_comm(self, device) -> int:
+        """Address of the group's NCCL communicator on `device` (0 under another backend). The
+        first call is collective: a barrier makes sure the communicator exists."""
+        if self._comm_ptr is None:
+            ptr = 0
+            if dist.get_backend(self.group) == "nccl":
+                dist.barrier(group=self.group, device_ids=[device.index])
+                group = self.group if self.group is not None else dist.group.WORLD
+                ptr = int(group._get_backend(device)._comm_ptr())
+            self._comm_ptr = ptr
+        return self._comm_ptr
+
     def step(self, q, qsl, seq_lens, scale):
         """p2p: this rank's split partials (o [S, n, Hq, D], lse [S, Hq, n]); nccl: every rank's
         combined partial (o [P, n, Hq, D], lse [P, Hq, n])."""
@@ -269,6 +283,9 @@ class ShardedFarMemory:
                 self.peer = PeerExchange(self.group, n=n, hq=hq, hd=d, device=q.device)
             return o_part, lse_part
         send, recv, o, lse = self._buffers(n, hq, d, q.device)
+        comm = self.nccl_comm(q.device)
+        if comm:  # combine + ncclAllGather, issued by the library
+            return kernels.allgather_partials(comm, o_part, lse_part, send, recv)
         kernels.combine(o_part, lse_part, o, lse)  # writes straight into the send buffer
         dist.all_gather_into_tensor(recv, send, group=self.group)
         return unpack_partials(recv, self.plan.world, n, hq, d)

@@ -200,6 +200,20 @@ int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplit
 int fold_combine(const float* o_part, const float* lse_part, int splits, float* o_out, float* lse_out, int n, int hq,
                  int hd, void* stream);
 
+/* The NCCL data plane of the sequence-sharded far read: each rank's partial, an all-gather over
+ * NVLink, then fold_merge. No reference counterpart (the reference runs on one GPU); it replaces
+ * the survey's fold_allgather_partials(comm, ...). Combines this rank's split partials o_part
+ * [splits, n, hq, hd] / lse_part [splits, hq, n] (as fold_combine) into one record {o [n, hq, hd],
+ * lse [hq, n]} in `send` (n*hq*hd + hq*n floats, 16-byte aligned) and all-gathers every rank's
+ * record into recv [world][n*hq*hd + hq*n] with ncclAllGather on `comm` (an ncclComm_t of the
+ * group, e.g. the communicator of PyTorch's ProcessGroupNCCL) on `stream`. fold_merge then merges
+ * the world records with the window read: out_f = recv with split stride n*hq*hd + hq*n, token
+ * stride hq*hd, head stride hd; lse_f = recv + n*hq*hd with the same split stride, head stride n,
+ * token stride 1. NCCL is looked up at the first call (the libnccl.so.2 already loaded in the
+ * process, else the system's); graph-capturable like any NCCL call. */
+int fold_allgather_partials(void* comm, const float* o_part, const float* lse_part, int splits, float* send,
+                            float* recv, int n, int hq, int hd, void* stream);
+
 /* Far read + merge that allocates nothing, for callers that cannot allocate device memory when
  * they run the draft step (an engine that plans every device buffer ahead of time and passes the
  * attention plugin only the step's tensors, a C runtime without a caching allocator). No
