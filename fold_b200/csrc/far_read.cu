@@ -22,35 +22,35 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarPa
   split_read<C, true>(nullptr, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
-// A window tile costs about this many far tiles (in tenths): the window read copies 16-byte chunks
-// with cp.async, which one SM issues at about half the rate TMA moves the far read's boxes.
-constexpr int kWindowTileCost10 = 23;
+// A window tile costs up to about this many far tiles (in tenths): the window read copies 16-byte
+// chunks with cp.async, which one SM issues at a lower rate than TMA moves the far read's boxes.
+// The estimate is on the high side on purpose: window blocks that finish early take far tiles.
+constexpr int kWindowTileCost10 = 40;
 
-// How many of a KV head's S blocks read the window in this step (the rest read the far memory),
-// from the device-side lengths: the count in [1, S - 1] whose slower side finishes first. Every
-// block of the launch computes the same count.
+// How many of a KV head's S blocks read the window in this step, from the device-side lengths:
+// the fewest whose window share stays within 3/4 of a block's average work. Every block of the
+// launch computes the same count.
 template <class C>
 __device__ __forceinline__ int window_blocks(const FarParams& far, const FarParams& win, int S) {
   const int qlen = far.qsl[1] - far.qsl[0];
   const int seq = far.seq[0];
   const int hist = max(seq - qlen, 0);
   int64_t pos0, end;
-  const int F = far_tiles<C::TK>(far, hist, &pos0, &end);
-  const int Wt = window_tiles<C::TK>(win, hist, seq, &pos0, &end);
-  int best = 1, best_t = 0x7fffffff;
-  for (int w = 1; w < S; ++w) {
-    const int tf = 10 * ((F + (S - w) - 1) / (S - w));
-    const int tw = kWindowTileCost10 * ((Wt + w - 1) / w);
-    const int t = tf > tw ? tf : tw;
-    if (t < best_t) best_t = t, best = w;
-  }
-  return best;
+  const int64_t F = far_tiles<C::TK>(far, hist, &pos0, &end);
+  const int64_t Wt = window_tiles<C::TK>(win, hist, seq, &pos0, &end);
+  const int64_t total = 10 * F + kWindowTileCost10 * Wt;  // all work of the head, tenths of a far tile
+  for (int w = 1; w < S - 1; ++w)
+    if (4 * kWindowTileCost10 * ((Wt + w - 1) / w) * S <= 3 * total) return w;
+  return max(S - 1, 1);
 }
 
-// The far read and the window read of one draft step in one launch: of the S = gridDim.x blocks
-// of KV head blockIdx.y, the first w (window_blocks) read the window into window slots [0, w) and
-// the others the far memory into far slots [0, S - w), so the window read (a few MB) runs beside
-// the far read instead of after it. Block (0, 0) stores w in plan[0] for the merge.
+// The far read and the window read of one draft step in one launch. Of the S = gridDim.x blocks of
+// KV head blockIdx.y, the first w (window_blocks) read the window into window slots [0, w); then
+// every block reads far tiles, which the head's blocks draw from a ticket counter
+// (split_read<DYN>) until none are left, into far slot blockIdx.x. So the window read (a few MB)
+// runs beside the far read, and the blocks that read it take fewer far tiles. Block (0, 0)
+// stores w in plan[0] for the merge; plan[1] counts finished blocks and plan[2 + h] is head h's
+// ticket counter: the last block to finish sets both back to zero for the next launch.
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     step_read_kernel(const __grid_constant__ CUtensorMap far_map, const FarParams far, const FarParams win,
@@ -58,10 +58,27 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   const int S = static_cast<int>(gridDim.x), x = static_cast<int>(blockIdx.x), h = static_cast<int>(blockIdx.y);
   const int w = window_blocks<C>(far, win, S);
   if (x == 0 && h == 0 && threadIdx.x == 0) *plan = w;
-  if (x < w)
+  if (x < w) {
     split_read<C, true>(nullptr, nullptr, win, x, h, w);
-  else
-    split_read<C, false>(&far_map, nullptr, far, x - w, h, S - w);
+    // The window read is done: its stage barriers are re-initialised for the far read (every
+    // phase is complete), and its generic shared-memory accesses are ordered before the far
+    // read's TMA writes into the same stages.
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int i = 0; i < C::NSTAGE; ++i) mbar_inval(stage_barriers<C>() + i);
+    __syncthreads();
+  }
+  split_read<C, false, true>(&far_map, nullptr, far, x, h, S);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this block's ticket draws, before it counts itself
+    const unsigned total = gridDim.x * gridDim.y;
+    if (static_cast<unsigned>(atomicAdd(plan + 1, 1)) == total - 1) {
+      for (unsigned i = 0; i < gridDim.y; ++i) atomicExch(plan + 2 + i, 0);
+      atomicExch(plan + 1, 0);
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -323,6 +340,7 @@ int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_h
                 "step read: this shape's far read takes the tcgen05 kernel (fold_far_read_kernel_for); issue "
                 "fold_far_read and fold_window_read");
   if (splits < 2) return fail(FOLD_ERR_INVALID_ARGUMENT, "step read: at least 2 blocks per KV head");
+  far.tickets = plan + 2;
   return with_mma_config(hd, rows, StepLaunch{far, win, side, pages, plan, static_cast<cudaStream_t>(stream)});
 }
 

@@ -37,7 +37,12 @@ struct FarParams {
   const int* block_table;
   int bt_len, num_blocks, block_size;
   int win_left, win_right, causal;
+  // Far read with tiles handed out per step (the step read): one ticket counter per KV head; each
+  // ticket is kTicketTiles consecutive tiles of that head. Zero before a launch, zero after it.
+  int* tickets;
 };
+
+constexpr int kTicketTiles = 2;
 
 constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100
 

@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
 // the far read's (pf, which also carries the output and the step geometry), and the two are merged
 // with the alpha weighting. Without far splits the output is the combined window read. With
 // `plan` (the step read's device word), the window set uses its first plan[0] slots and the far
-// set its first pw.splits - plan[0].
+// set all of its slots (a block that drew no far tile left an empty partial).
 __global__ void __launch_bounds__(kMergeWarps * 32)
     merge_partials_kernel(const MergeParams pw, const MergeParams pf, const int* plan, int slices, int hd) {
   __shared__ SliceSums sums;
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   const bool active = lane * 4 < min(hd, kSlice);
   const int col = slice * kSlice + lane * 4;
   const int wsplits = plan ? min(max(*plan, 0), pw.splits) : pw.splits;
-  const int fsplits = plan ? pw.splits - wsplits : pf.splits;
+  const int fsplits = pf.splits;
   float ol[4], ll;
   combine_slice(pw, t, h, col, active, true, sums, ol, ll, wsplits);
   float of[4] = {0.f, 0.f, 0.f, 0.f}, lf = -INFINITY;

@@ -265,21 +265,39 @@ __device__ __forceinline__ int window_tiles(const FarParams& p, int hist, int se
   return u_hi > u_lo ? static_cast<int>((u_hi + TK - 1) / TK - t0) : 0;
 }
 
+// The mbarriers of a CTA's stage ring (in the dynamic shared memory of a split read).
+template <class C>
+__device__ __forceinline__ uint64_t* stage_barriers() {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  return reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+}
+
 // The split-KV read of one (split of nsplits, KV head h), in two modes.
 //   WIN = false, far memory: K|V rows of the side cache through `map`, the query rotated to the
 //     shared far position, row r reads positions [0, H - W - B + 1 + r) (fold/attention.py:164).
 //   WIN = true, window read: K and V rows of the paged cache (p.kc, p.vc, cp.async by every
 //     thread), the query as given, row r reads its exact-position window
 //     (fold/attention.py:148-151,163).
-template <class C, bool WIN>
+// DYN (far memory only): instead of the fixed range of split `split`, the CTA takes its tiles
+// from the head's ticket counter (p.tickets[h]), kTicketTiles at a time, until the head's tiles
+// are all taken; `split` is then only the slot of its partial. Thread 0 draws the tickets (one
+// ticket ahead, so that the atomic's latency is off the refill path) and records each stage's tile
+// in shared memory beside the stage's mbarrier; a stage marked -1 (completed by a plain arrival)
+// ends the loop for every warp.
+template <class C, bool WIN, bool DYN = false>
 __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
                                            int split, int h, int nsplits) {
+  static_assert(!(WIN && DYN), "tiles by ticket are for the far read");
   constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
   constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  volatile int* st_tile = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * C::NSTAGE);  // DYN
+  static_assert(C::NSTAGE * 12 <= 64, "stage barriers and tiles share 64 bytes");
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_Q);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
   float* row_m = reinterpret_cast<float*>(smem + C::OFF_ROW);
@@ -308,6 +326,31 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   // Window read: lane 0 of each warp holds the block of the warp's rows in the next tile to be
   // issued (looked up one tile ahead, so that the lookup's latency is off the refill's path).
   int next_blk = -1;
+  // DYN, thread 0: the tiles [cur_t, cur_end) left of the current ticket, the ticket drawn ahead,
+  // stages filled so far (markers included), and whether the end marker has been written.
+  int cur_t = 0, cur_end = 0, next_ticket = 0, filled = 0;
+  bool exhausted = false;
+  auto grab = [&]() -> int {  // the CTA's next tile, or -1 once the head's tiles are all taken
+    if (cur_t >= cur_end) {
+      cur_t = next_ticket * kTicketTiles;
+      cur_end = min(cur_t + kTicketTiles, tiles);
+      if (cur_t >= tiles) return -1;
+      next_ticket = atomicAdd(p.tickets + h, 1);
+    }
+    return cur_t++;
+  };
+  // DYN, thread 0: fills stage st with the next tile, or with the end marker.
+  auto fill = [&](int st) {
+    const int t = grab();
+    st_tile[st] = t;
+    ++filled;
+    if (t < 0) {
+      exhausted = true;
+      mbar_arrive(&full[st]);
+    } else {
+      issue_tile<C>(smem, full, map, st, t, p.hkv, h, pol);
+    }
+  };
   // Tile t of this cache into stage st: far read by thread 0 (TMA), window read by every thread.
   auto issue = [&](int st, int t) {
     if constexpr (WIN) {
@@ -334,7 +377,12 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       // Fill the ring right away, so the first copies overlap the query rotation below.
       pol = l2_evict_first_policy();
       prefetch_tensormap(map);
-      for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
+      if constexpr (DYN) {
+        next_ticket = atomicAdd(p.tickets + h, 1);
+        for (int i = 0; i < NSTAGE && !exhausted; ++i) fill(i);
+      } else {
+        for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
+      }
     }
   }
 
@@ -461,12 +509,17 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   int consumed = 0;
   const uint32_t p_base = smem_u32(smem + C::OFF_P);
 
-  for (int it = 0; it < ntiles; ++it) {
+  for (int it = 0; DYN || it < ntiles; ++it) {
     const int st = it % NSTAGE;
     const bool ok = mbar_wait(&full[st], (it / NSTAGE) & 1);
+    int tile = t_begin + it;  // this tile's index in the cache
+    if constexpr (DYN) {
+      tile = st_tile[st];  // written by thread 0 before it armed the stage
+      if (tile < 0) break;  // the end marker: the same stage, so the same decision, in every warp
+    }
     const uint32_t kv_base = smem_u32(smem + st * C::STAGE_BYTES);
     const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
-    const int64_t tpos = pos0 + static_cast<int64_t>(t_begin + it) * TK;  // first position of the tile
+    const int64_t tpos = pos0 + static_cast<int64_t>(tile) * TK;  // first position of the tile
     const int64_t key0 = tpos + mt * 16 + g4;
 
     float x[QNT][4];
@@ -550,8 +603,11 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     // One barrier per tile: P^T of every warp is written, every warp is done with the previous
     // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
     const bool attention = named_bar_or(exceed || !ok, 1, NTH);
-    if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles)
+    if constexpr (DYN) {
+      if (tid == 0 && it >= 1 && !exhausted) fill((it - 1) % NSTAGE);
+    } else if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles) {
       issue((it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE);
+    }
     if (attention) {
       if (named_bar_or(!ok, 2, NTH)) {
         timed_out = true;
@@ -666,7 +722,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     if constexpr (WIN) {
       cp_async_wait_all();
     } else if (tid == 0) {
-      const int issued = min(ntiles, max(consumed, 1) - 1 + NSTAGE);
+      const int issued = DYN ? filled : min(ntiles, max(consumed, 1) - 1 + NSTAGE);
       for (int i = consumed; i < issued; ++i)
         if (!mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1)) break;
     }

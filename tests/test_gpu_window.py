@@ -153,14 +153,14 @@ def test_merge_partials_matches_oracle_fold_step(hist):
     S = kernels.default_splits(hkv)
     far = (torch.empty((S, n, hq, hd), device="cuda"), torch.empty((S, hq, n), device="cuda"))
     win = (torch.empty((S, n, hq, hd), device="cuda"), torch.empty((S, hq, n), device="cuda"))
-    plan = torch.zeros(1, dtype=torch.int32, device="cuda")
+    plan = torch.zeros(2 + hkv, dtype=torch.int32, device="cuda")
     kernels.step_read(qd, qd, qsl, seq_t, side, far, kc, vc, table, win, plan, window=W, block=B, far_distance=W + B,
                       softmax_scale=scale, alpha=alpha, window_size=(W + B - 1, B - 1), causal=False, table=tab)
     out2 = torch.empty_like(out)
     kernels.merge_partials(win[0], win[1], far[0], far[1], out2, qsl, seq_t, window=W, block=B, alpha=alpha,
                            plan=plan)
     torch.cuda.synchronize()
-    assert 1 <= int(plan.item()) < S
+    assert 1 <= int(plan[0].item()) < S
     assert np.abs(to64(out2) - want).max() <= OUT_ATOL
 
 
@@ -168,9 +168,12 @@ def test_merge_partials_matches_oracle_fold_step(hist):
                                               (128, 32, 8, 8, 32760), (256, 16, 8, 8, 9000),
                                               (128, 32, 8, 10, 1500)])  # last: no far key at all
 def test_step_read_equals_separate_reads(hd, hq, hkv, n, hist, far_kernel):
-    """The one-launch step read splits each KV head's S blocks into w window and S - w far blocks
-    (plan[0] = w) and writes bit for bit the partials of fold_window_read with w splits and of
-    fold_far_read with S - w splits. Shapes whose far read takes the tcgen05 kernel are refused."""
+    """The one-launch step read: w of each KV head's S blocks (plan[0] = w) write bit for bit the
+    partials of fold_window_read with w splits; then all S blocks draw the head's far tiles from
+    its ticket counter, and their S far slots together hold the far read: combined, they equal the
+    combine of fold_far_read's S partials (to float32 rounding of a different summation order).
+    The step leaves its block count and tickets at zero, so a second launch reads the same. Shapes
+    whose far read takes the tcgen05 kernel are refused."""
     from fold_b200.errors import FoldError
 
     rng = np.random.default_rng(hd + hist)
@@ -195,22 +198,28 @@ def test_step_read_equals_separate_reads(hd, hq, hkv, n, hist, far_kernel):
 
     S = kernels.default_splits(hkv)
     far_a, win_a = bufs(S), bufs(S)
-    plan = torch.zeros(1, dtype=torch.int32, device="cuda")
+    plan = torch.zeros(2 + hkv, dtype=torch.int32, device="cuda")
     args = dict(window=W, block=B, far_distance=W + B, softmax_scale=scale, alpha=alpha, window_size=ws,
                 causal=False, table=tab)
     if kernels.far_read_uses_tcgen05(hd, n, hq, hkv):
         with pytest.raises(FoldError, match="tcgen05"):
             kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, plan, **args)
         return
-    kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, plan, **args)
-    torch.cuda.synchronize()
-    w = int(plan.item())
-    assert 1 <= w < S
-    far_b, win_b = bufs(S - w), bufs(w)
+    far_b = bufs(S)
     kernels.far_read(qd, qsl, seq_t, side, far_b[0], far_b[1], window=W, block=B, far_distance=W + B,
                      softmax_scale=scale * alpha, table=tab)
-    kernels.window_read(qd, qsl, seq_t, kc, vc, table, win_b[0], win_b[1], window_size=ws, causal=False,
-                        softmax_scale=scale)
-    torch.cuda.synchronize()
-    assert torch.equal(far_a[0][: S - w], far_b[0]) and torch.equal(far_a[1][: S - w], far_b[1])
-    assert torch.equal(win_a[0][:w], win_b[0]) and torch.equal(win_a[1][:w], win_b[1])
+    o_b, l_b = kernels.combine(far_b[0], far_b[1])
+    for launch in range(2):
+        kernels.step_read(qd, qd, qsl, seq_t, side, far_a, kc, vc, table, win_a, plan, **args)
+        torch.cuda.synchronize()
+        w = int(plan[0].item())
+        assert 1 <= w < S
+        assert int(plan[1:].abs().sum().item()) == 0, f"launch {launch}: counters not reset"
+        win_b = bufs(w)
+        kernels.window_read(qd, qsl, seq_t, kc, vc, table, win_b[0], win_b[1], window_size=ws, causal=False,
+                            softmax_scale=scale)
+        o_a, l_a = kernels.combine(far_a[0], far_a[1])
+        torch.cuda.synchronize()
+        assert torch.equal(win_a[0][:w], win_b[0]) and torch.equal(win_a[1][:w], win_b[1])
+        assert np.abs(to64(o_a) - to64(o_b)).max() <= 5e-3
+        lse_close(to64(l_a), to64(l_b), rtol=1e-4)
