@@ -55,7 +55,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="fold", choices=["fold", "reference"])
+    ap.add_argument("--impl", default="fold", choices=["fold", "reference", "fa4"],
+                    help="fold: this library; reference: the CPU implementation of the path; fa4: the "
+                         "reference's own GPU path (its Triton rotation and merge with FlashAttention-4) alone")
+    ap.add_argument("--no-fa4", action="store_true", help="skip timing the reference's GPU path beside the step")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0, help="far-read splits per KV head (0: one CTA per SM)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -443,6 +446,10 @@ def run_gpu(args):
         del alt_graph
     window = run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err,
                         append) if world == 1 else None
+    fa4 = None
+    if world == 1 and (args.impl == "fa4" or not args.no_fa4):
+        fa4 = run_fa4(args, cfg, dev, stream, side, q_all, seq_all, qsl, new_k, new_v, new_pos, acc, o_l, lse_l,
+                      length, inv)
     # every rank takes part in the reduction before any rank may raise (same collectives everywhere)
     t = torch.tensor([ms, far_ms, far_sustained_ms, float(err.item()), alt_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -514,6 +521,17 @@ def run_gpu(args):
         }
         if window is not None:
             line["window_read"] = window
+        if fa4 is not None:
+            line["reference_gpu_path"] = fa4
+        if args.impl == "fa4":  # the reference's GPU path as its own line
+            ok = "us_per_step" in fa4
+            line = {"impl": "fa4", "metric": METRIC, "value": fa4.get("us_per_step"), "unit": "us/draft-step",
+                    "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(fa4["us_per_step"] / 1000, 6) if ok else None, "higher_is_better": False,
+                    "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": line["data"],
+                    "config": line["config"], "reference_gpu_path": fa4}
+            if not ok:
+                line = {"impl": "fa4", "unavailable": fa4.get("unavailable")}
         if alt is not None:
             line["exchange_alternative"] = {
                 "exchange": alt, "us_per_step": round(1000.0 * alt_ms / args.steps, 3),
@@ -529,6 +547,106 @@ def run_gpu(args):
         peer.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_fa4(args, cfg, dev, stream, side, q_all, seq_all, qsl, new_k, new_v, new_pos, acc, o_l, lse_l, length, inv):
+    """The reference's own GPU path for the same steps (fold/attention.py:162-172, 260-265): the
+    side-cache scatter of _wrap_context_kv in torch, its Triton far_query, FlashAttention-4 over the
+    side cache (paged, causal, seqused_k = far_len, num_splits = max(16, 64 // Hkv)) and its
+    Triton merge, from the unmodified reference package installed under baseline/_ref and vLLM's
+    flash_attn_varlen_func(fa_version=4). Timed like the step: one CUDA graph of K steps after
+    0.3 s of load, CUDA events. Returns the result dict, or {"unavailable": why}."""
+    import torch
+
+    try:
+        ref_path = ROOT / "baseline" / "_ref"
+        if not (ref_path / "fold" / "kernels.py").exists():
+            return {"unavailable": "the reference is not installed under baseline/_ref"}
+        if str(ref_path) not in sys.path:
+            sys.path.insert(0, str(ref_path))
+        from fold.kernels import far_query, merge  # noqa: PLC0415
+        from vllm.vllm_flash_attn import fa_version_unsupported_reason, flash_attn_varlen_func  # noqa: PLC0415
+        why = fa_version_unsupported_reason(4)
+        if why:
+            return {"unavailable": f"FlashAttention-4: {why}"}
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
+    pages = side.shape[0]
+    side_table = torch.arange(pages, device=dev, dtype=torch.int32)[None]
+    far_len = torch.zeros(1, device=dev, dtype=torch.int32)
+    fk, fv = side.transpose(1, 2).split(hd, dim=-1)
+    out = torch.empty((B, hq * hd), device=dev, dtype=torch.bfloat16)
+    splits = max(16, 64 // hkv)
+    scale = hd ** -0.5 * ALPHA
+
+    def append(i):
+        a = int(acc[i - 1]) if i > 0 else 0
+        if a:
+            pos = new_pos[i - 1, :a]
+            pg, off = torch.div(pos, 256, rounding_mode="floor"), pos % 256
+            side[pg, :, off, :hd] = new_k[i - 1, :a]
+            side[pg, :, off, hd:] = new_v[i - 1, :a]
+
+    def far(i, qf):
+        return flash_attn_varlen_func(q=qf, k=fk, v=fv, cu_seqlens_q=qsl, max_seqlen_q=B, seqused_k=far_len,
+                                      max_seqlen_k=length, softmax_scale=scale, causal=True, block_table=side_table,
+                                      return_softmax_lse=True, fa_version=4, num_splits=splits)
+
+    def step(i):
+        append(i)
+        seq = seq_all[i: i + 1]
+        qf = far_query(q_all[i], qsl, seq, inv, far_len, far_distance=W + B, window=W, block=B)
+        out_f, lse_f = far(i, qf)
+        merge(o_l, lse_l, out_f, lse_f, out.view(B, hq, hd), qsl, seq, window=W, block=B, alpha=ALPHA)
+
+    try:
+        t_first = time.perf_counter()
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        first_s = time.perf_counter() - t_first
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def graph_of(fn):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for j in range(args.steps):
+                    fn(args.warmup + j)
+            g.replay()
+            torch.cuda.synchronize()
+            return g
+
+        def timed(g, sustained):
+            if sustained:
+                t0 = time.perf_counter()
+                while time.perf_counter() - t0 < 0.3:
+                    g.replay()
+                    torch.cuda.synchronize()
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            return 1000.0 * e0.elapsed_time(e1) / args.steps
+
+        qf_fixed = far_query(q_all[args.warmup], qsl, seq_all[args.warmup: args.warmup + 1], inv, far_len,
+                             far_distance=W + B, window=W, block=B)
+        gf = graph_of(lambda i: far(i, qf_fixed))
+        far_burst = timed(gf, False)
+        far_sustained = timed(gf, True)
+        del gf
+        gs = graph_of(step)
+        us = timed(gs, True)
+        del gs
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    return {"us_per_step": round(us, 3), "unit": "us/draft-step",
+            "far_read_us_sustained": round(far_sustained, 3), "far_read_us_burst": round(far_burst, 3),
+            "first_calls_s": round(first_s, 1), "splits": splits,
+            "path": "reference GPU path: torch side-cache scatter + Triton far_query + FlashAttention-4 far read "
+                    "(vllm.vllm_flash_attn, fa_version=4) + Triton merge, unmodified from baseline/_ref",
+            "timing": "one CUDA graph of K steps after 0.3 s of back-to-back replays (sustained), CUDA events; "
+                      "the far read alone likewise, burst and sustained"}
 
 
 def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err, append):
@@ -947,6 +1065,8 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     else:
+        if args.impl == "fa4":
+            args.no_e2e = args.no_cpu = True
         run_gpu(args)
 
 

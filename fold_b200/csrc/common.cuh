@@ -133,6 +133,37 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D += A(16x16, row) * B(16x8, col), f16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two floats rounded to f16 (nearest even; magnitudes past the f16 range saturate at +-65504),
+// `lo` in the low half.
+__device__ __forceinline__ uint32_t pack_f16_sat(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// The two f16 halves of a packed pair as floats (low half first).
+__device__ __forceinline__ float2 unpack_f16(uint32_t x) {
+  float2 v;
+  asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+      : "=f"(v.x), "=f"(v.y)
+      : "r"(x));
+  return v;
+}
+// A packed bf16 pair re-encoded as an f16 pair (exact in the f16 normal range; magnitudes past it
+// saturate at +-65504, values below it become f16 subnormals or zero).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+  return pack_f16_sat(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

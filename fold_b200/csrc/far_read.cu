@@ -46,11 +46,11 @@ __device__ __forceinline__ int window_blocks(const FarParams& far, const FarPara
 
 // The far read and the window read of one draft step in one launch. Of the S = gridDim.x blocks of
 // KV head blockIdx.y, the first w (window_blocks) read the window into window slots [0, w); then
-// every block reads far tiles, which the head's blocks draw from a ticket counter
+// every block reads far tiles, which the head's blocks draw in grants from a tile counter
 // (split_read<DYN>) until none are left, into far slot blockIdx.x. So the window read (a few MB)
 // runs beside the far read, and the blocks that read it take fewer far tiles. Block (0, 0)
 // stores w in plan[0] for the merge; plan[1] counts finished blocks and plan[2 + h] is head h's
-// ticket counter: the last block to finish sets both back to zero for the next launch.
+// tile counter: the last block to finish sets both back to zero for the next launch.
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     step_read_kernel(const __grid_constant__ CUtensorMap far_map, const FarParams far, const FarParams win,

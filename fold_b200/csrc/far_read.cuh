@@ -8,8 +8,10 @@
 
 namespace fold {
 
-// Lazy row-maximum threshold (log2 units), see far_read.cu.
-constexpr float kRaise = 16.0f;
+// Lazy row-maximum threshold (log2 units): the running maximum of a row only moves when a logit
+// passes it by more than this, so P = 2^(logit - maximum) stays below 2^15 and fits f16 (whose
+// largest finite value is 65504).
+constexpr float kRaise = 15.0f;
 
 struct FarParams {
   const __nv_bfloat16* q;
@@ -37,12 +39,12 @@ struct FarParams {
   const int* block_table;
   int bt_len, num_blocks, block_size;
   int win_left, win_right, causal;
-  // Far read with tiles handed out per step (the step read): one ticket counter per KV head; each
-  // ticket is kTicketTiles consecutive tiles of that head. Zero before a launch, zero after it.
+  // Far read with tiles handed out per step (the step read): one counter per KV head of the tiles
+  // granted so far. Zero before a launch, zero after it.
   int* tickets;
 };
 
-constexpr int kTicketTiles = 2;
+constexpr int kTicketTiles = 2;  // the smallest grant of tiles
 
 constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100
 

@@ -16,7 +16,11 @@
 //   Q        K-major, 128-byte swizzle, written by the rotation prologue;
 //   V^T      MN-major, 128-byte swizzle: the same TMA boxes read with hd as the M dimension;
 //   P^T      MN-major, no swizzle: [row group of 8][key][8 rows] bf16, so each softmax thread
-//            stores 16-byte vectors.
+//            stores 16-byte vectors. P is split into a bf16 high part and the bf16 rounding of
+//            the rest (two buffers of that layout), and O^T += V^T . P^T takes one MMA for each:
+//            P then carries 16 significant bits. A bf16 P alone (8 bits) put its rounding of the
+//            weights of a few dominant keys straight into the output, 0.03-0.05 on the x8
+//            outlier channels of the 128K Llama workload. The row sums add the same two parts.
 // Every mbarrier wait is bounded (FOLD_DEVERR_TIMEOUT); TMEM is freed on every exit path.
 #include <cuda_bf16.h>
 
@@ -188,7 +192,8 @@ struct TcCfg {
   static constexpr int NTHREADS = NSM + 64;
   static constexpr int Q_CHUNK = NP * 128;  // 64 columns of Q, swizzled
   static constexpr int Q_BYTES = (HD / 64) * Q_CHUNK;
-  static constexpr int P_BYTES = NP * TK * 2;
+  static constexpr int P_HALF = NP * TK * 2;  // one bf16 part of P^T
+  static constexpr int P_BYTES = 2 * P_HALF;   // high and low parts
   static constexpr int RED_BYTES = NSW * NP * 4;
   static constexpr int ROW_BYTES = 3 * NP * 4;  // row limits, row maxima, rescale factors
   static constexpr int NBAR = 26;
@@ -487,9 +492,12 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
             const uint32_t v = slot_base + (u % NSLOT) * C::UNIT_BYTES;
 #pragma unroll
             for (int ks = 0; ks < TK / 16; ++ks) {
-              tc_mma(tmem + C::TMEM_O + hh * NP, smem_desc(v + ks * 2048, C::BOX_BYTES, 1024, kSwizzle128),
-                     smem_desc(p_base + (t % C::P_BUFS) * C::P_BYTES + ks * 256, 128, TK * 16, kSwizzleNone),
-                     idesc_o, (t > 0 || ks > 0));
+              const uint64_t vd = smem_desc(v + ks * 2048, C::BOX_BYTES, 1024, kSwizzle128);
+              const uint32_t pp = p_base + (t % C::P_BUFS) * C::P_BYTES + ks * 256;
+              tc_mma(tmem + C::TMEM_O + hh * NP, vd, smem_desc(pp, 128, TK * 16, kSwizzleNone), idesc_o,
+                     (t > 0 || ks > 0));
+              tc_mma(tmem + C::TMEM_O + hh * NP, vd, smem_desc(pp + C::P_HALF, 128, TK * 16, kSwizzleNone), idesc_o,
+                     1u);
             }
           }
           tc_commit(&pv_done[b]);
@@ -589,18 +597,21 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
       unsigned char* pb = smem + p_base_gen + (i % C::P_BUFS) * C::P_BYTES + tid * 16;
 #pragma unroll
       for (int g = 0; g < NP / 8; ++g) {
-        uint32_t w[4];
+        uint32_t w[4], wl[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = g * 8 + 2 * j;
           const float m0 = rowm[c] == -INFINITY ? 0.f : rowm[c];
           const float m1 = rowm[c + 1] == -INFINITY ? 0.f : rowm[c + 1];
           const float p0 = fast_exp2(x[c] - m0), p1 = fast_exp2(x[c + 1] - m1);
-          l[c] += p0;
-          l[c + 1] += p1;
-          w[j] = pack_bf16(p0, p1);
+          w[j] = pack_bf16(p0, p1);  // high parts
+          const float h0 = __uint_as_float(w[j] << 16), h1 = __uint_as_float(w[j] & 0xffff0000u);
+          wl[j] = pack_bf16(p0 - h0, p1 - h1);  // the rest, rounded (exact differences)
+          l[c] += h0 + __uint_as_float(wl[j] << 16);
+          l[c + 1] += h1 + __uint_as_float(wl[j] & 0xffff0000u);
         }
         *reinterpret_cast<uint4*>(pb + g * TK * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(pb + C::P_HALF + g * TK * 16) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
       }
       fence_proxy_async();  // P^T is read by the tensor cores
       tc_fence_before();

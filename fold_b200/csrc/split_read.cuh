@@ -12,13 +12,22 @@
 //   S^T = K . Qf^T     (keys on the MMA M dimension, the n*G query rows on N: no row padding)
 //   P^T = exp2(S^T * scale * log2e - m)      (online softmax with a lazily raised row maximum)
 //   O^T += V^T . P^T
-// on bf16 mma.sync tiles, and finally write the split's normalised partial (o, lse).
+// on mma.sync tiles (bf16 for S^T, f16 for O^T), and finally write the split's normalised partial
+// (o, lse).
 //
 // The running row maximum m only moves when a new logit exceeds it by more than kRaise (log2
 // units), which is decided for the whole CTA by one OR-barrier per tile. So the common tile needs
-// no cross-warp max exchange and no rescaling. P stays below 2^kRaise: bf16 keeps its 8-bit
-// mantissa at any magnitude and the fp32 sums of at most 2^16 * (keys per split) stay far from
-// overflow, so a high threshold costs no accuracy and makes raises rare after the first tile.
+// no cross-warp max exchange and no rescaling. P stays below 2^kRaise, inside the f16 range, and
+// the fp32 sums of at most 2^15 * (keys per split) stay far from overflow, so a high threshold
+// costs no accuracy and makes raises rare after the first tile.
+//
+// P is rounded to f16 (11 significant bits) for the PV product, and the row sums add the rounded
+// values, so the weights that multiply V sum to exactly the normaliser. With bf16 P (8 bits), a
+// row whose mass sits on a few keys carried the rounding of those weights straight into the
+// output: 0.03-0.05 on the x8 outlier channels of the 128K Llama workload. V tiles are bf16 in
+// memory; their MMA fragments are re-encoded as f16 in registers (exact in the f16 range; the
+// conversion saturates at +-65504), since an MMA takes both operands in one type. Q and K stay
+// bf16 for S^T = K . Q^T.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -281,11 +290,13 @@ __device__ __forceinline__ uint64_t* stage_barriers() {
 //     thread), the query as given, row r reads its exact-position window
 //     (fold/attention.py:148-151,163).
 // DYN (far memory only): instead of the fixed range of split `split`, the CTA takes its tiles
-// from the head's ticket counter (p.tickets[h]), kTicketTiles at a time, until the head's tiles
-// are all taken; `split` is then only the slot of its partial. Thread 0 draws the tickets (one
-// ticket ahead, so that the atomic's latency is off the refill path) and records each stage's tile
-// in shared memory beside the stage's mbarrier; a stage marked -1 (completed by a plain arrival)
-// ends the loop for every warp.
+// from the head's tile counter (p.tickets[h]) in grants until the head's tiles are all taken;
+// `split` is then only the slot of its partial. A grant is the tiles left after the CTA's current
+// one divided by twice the CTA count (guided self-scheduling, at least kTicketTiles), so a CTA
+// draws a handful of grants, large ones first and small ones at the end. Thread 0 draws them one
+// grant ahead, so that the atomic's latency stays off the refill path, and records each stage's
+// tile in shared memory beside the stage's mbarrier; a stage marked -1 (completed by a plain
+// arrival) ends the loop for every warp.
 template <class C, bool WIN, bool DYN = false>
 __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
                                            int split, int h, int nsplits) {
@@ -326,16 +337,19 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   // Window read: lane 0 of each warp holds the block of the warp's rows in the next tile to be
   // issued (looked up one tile ahead, so that the lookup's latency is off the refill's path).
   int next_blk = -1;
-  // DYN, thread 0: the tiles [cur_t, cur_end) left of the current ticket, the ticket drawn ahead,
-  // stages filled so far (markers included), and whether the end marker has been written.
-  int cur_t = 0, cur_end = 0, next_ticket = 0, filled = 0;
+  // DYN, thread 0: the tiles [cur_t, cur_end) left of the current grant, the grant drawn ahead
+  // (first tile and size), stages filled so far (markers included), and whether the end marker
+  // has been written.
+  int cur_t = 0, cur_end = 0, next_start = 0, next_take = 0, filled = 0;
   bool exhausted = false;
+  auto grant_size = [&](int seen) { return max(kTicketTiles, (tiles - seen) / (2 * nsplits)); };
   auto grab = [&]() -> int {  // the CTA's next tile, or -1 once the head's tiles are all taken
     if (cur_t >= cur_end) {
-      cur_t = next_ticket * kTicketTiles;
-      cur_end = min(cur_t + kTicketTiles, tiles);
+      cur_t = next_start;
+      cur_end = min(next_start + next_take, tiles);
       if (cur_t >= tiles) return -1;
-      next_ticket = atomicAdd(p.tickets + h, 1);
+      next_take = grant_size(cur_end);
+      next_start = atomicAdd(p.tickets + h, next_take);
     }
     return cur_t++;
   };
@@ -378,7 +392,8 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       pol = l2_evict_first_policy();
       prefetch_tensormap(map);
       if constexpr (DYN) {
-        next_ticket = atomicAdd(p.tickets + h, 1);
+        next_take = grant_size(0);
+        next_start = atomicAdd(p.tickets + h, next_take);
         for (int i = 0; i < NSTAGE && !exhausted; ++i) fill(i);
       } else {
         for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
@@ -585,16 +600,16 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         for (int j = 0; j < QNT; ++j) {
           const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
           const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-          const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
-          const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
-          ls[j][0] = p0 + p2;
-          ls[j][1] = p1 + p3;
+          const uint32_t pa = pack_f16_sat(fast_exp2(x[j][0] - m0), fast_exp2(x[j][1] - m1));
+          const uint32_t pb = pack_f16_sat(fast_exp2(x[j][2] - m0), fast_exp2(x[j][3] - m1));
+          const float2 ra = unpack_f16(pa), rb = unpack_f16(pb);
+          ls[j][0] = ra.x + rb.x;
+          ls[j][1] = ra.y + rb.y;
           if (nt_lo + j < NT) {
             const int r0 = (nt_lo + j) * 8 + t4 * 2;
             const int k0 = mt * 16 + g4;
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2),
-                         "r"(pack_bf16(p2, p3)));
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pa));
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pb));
           }
         }
       }
@@ -666,15 +681,16 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         }
         const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
         const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
-        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
-        ls[j][0] = p0 + p2;
-        ls[j][1] = p1 + p3;
+        const uint32_t pa = pack_f16_sat(fast_exp2(x[j][0] - m0), fast_exp2(x[j][1] - m1));
+        const uint32_t pb = pack_f16_sat(fast_exp2(x[j][2] - m0), fast_exp2(x[j][3] - m1));
+        const float2 ra = unpack_f16(pa), rb = unpack_f16(pb);
+        ls[j][0] = ra.x + rb.x;
+        ls[j][1] = ra.y + rb.y;
         if (nt_lo + j < NT) {
           const int r0 = (nt_lo + j) * 8 + t4 * 2;
           const int k0 = mt * 16 + g4;
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p0, p1)));
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pack_bf16(p2, p3)));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pa));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pb));
         }
       }
       named_bar_sync(2, NTH);
@@ -707,8 +723,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
             kv_base + (C::KBOX + (ht >> 2)) * C::BOX_BYTES + key_row * 128 + ((chunk ^ (key_row & 7)) << 4);
         uint32_t a0, a1, a2, a3;
         ldsm_x4_t(va, a0, a1, a2, a3);
+        a0 = bf16x2_to_f16x2(a0), a1 = bf16x2_to_f16x2(a1), a2 = bf16x2_to_f16x2(a2), a3 = bf16x2_to_f16x2(a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_bf16(oacc[a][nt], a0, a1, a2, a3, bfr[nt][0], bfr[nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_f16(oacc[a][nt], a0, a1, a2, a3, bfr[nt][0], bfr[nt][1]);
       }
     }
     consumed = it + 1;

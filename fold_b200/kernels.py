@@ -319,10 +319,12 @@ def append(k, v, positions, slots, side, *, pos_lo=0, skip_foreign=False, err=No
         raise FoldError("append: K/V must be [ctx, Hkv, head_dim] matching the side cache")
     if k.stride(-1) != 1 or v.stride(-1) != 1:
         raise FoldError("append: the head dimension of K and V must be contiguous")
-    if positions.shape[0] != ctx or positions.dtype != torch.int64:
-        positions = positions[:ctx].to(torch.int64)
-    if slots.shape[0] != ctx or slots.dtype != torch.int64:
-        slots = slots[:ctx].to(torch.int64)
+    if positions.dim() != 1 or slots.dim() != 1 or positions.shape[0] < ctx or slots.shape[0] < ctx:
+        raise FoldError("append: positions and slots need one entry per K/V row")
+    if positions.shape[0] != ctx or positions.dtype != torch.int64 or not positions.is_contiguous():
+        positions = positions[:ctx].to(torch.int64).contiguous()
+    if slots.shape[0] != ctx or slots.dtype != torch.int64 or not slots.is_contiguous():
+        slots = slots[:ctx].to(torch.int64).contiguous()
     _lib.call("fold_append", _p(k), k.stride(0), k.stride(1), _p(v), v.stride(0), v.stride(1), _p(positions),
               _p(slots), ctx, _p(side), pages, hkv, d2 // 2, int(pos_lo), int(bool(skip_foreign)), _p(err),
               _stream(side))

@@ -74,6 +74,23 @@ def test_append_sharded_skips_foreign_positions_and_gather_round_trips():
     assert int(err.item()) == 1
 
 
+def test_append_rejects_positions_shorter_than_the_rows():
+    """Every K/V row needs its position and slot: shorter arrays are refused (the kernel would
+    read past them), longer ones are cut to the rows."""
+    from fold_b200.errors import FoldError
+    side = torch.zeros((3, 2, 256, 256), device="cuda", dtype=torch.bfloat16)
+    k = torch.randn((8, 2, 128), device="cuda").to(torch.bfloat16)
+    pos = torch.arange(8, device="cuda")
+    with pytest.raises(FoldError, match="one entry per K/V row"):
+        kernels.append(k, k, pos[:7], pos, side)
+    with pytest.raises(FoldError, match="one entry per K/V row"):
+        kernels.append(k, k, pos, pos[:5], side)
+    kernels.append(k, k, torch.arange(12, device="cuda"), torch.arange(12, device="cuda"), side)
+    kg, _ = kernels.gather(side, pos)
+    torch.cuda.synchronize()
+    assert torch.equal(kg, k)
+
+
 # ---------------------------------------------------------------------------------- far query
 @pytest.mark.parametrize("n,hq,hd,rot,hist,D", [(10, 32, 128, 128, 131062, 2058), (8, 4, 128, 64, 100000, 2056),
                                                (4, 4, 64, 64, 30, 44), (3, 2, 256, 256, 262000, 4112)])

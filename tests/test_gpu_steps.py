@@ -70,8 +70,9 @@ def test_two_hundred_draft_steps_match_oracle():
     ws = FoldWorkspace(dummy, W, B, length, inv_freq=inv, far_distance=W + B, alpha=ALPHA, num_heads=HQ)
     # the prefill: committed context appended in chunks, as precompute_and_store_context_kv does
     for a in range(0, H0, 8192):
-        pos = torch.arange(a, min(H0, a + 8192), device="cuda")
-        ws.append(bf16_tensor(k_raw[a:a + 8192]), bf16_tensor(v_raw[a:a + 8192]), pos, pos)
+        b = min(H0, a + 8192)
+        pos = torch.arange(a, b, device="cuda")
+        ws.append(bf16_tensor(k_raw[a:b]), bf16_tensor(v_raw[a:b]), pos, pos)
     original = SimpleNamespace(head_size=HD, scale=HD ** -0.5, num_heads=HQ, sliding_window=(-1, -1),
                                vllm_flash_attn_version=4)
     layer = FoldAttention(original, ws)
