@@ -677,7 +677,7 @@ def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_
     fsplits = max(kernels.default_splits(hkv), 2)  # blocks per KV head, shared by the two reads
     far_parts = (torch.empty((fsplits, B, hq, hd), device=dev), torch.empty((fsplits, hq, B), device=dev))
     win_parts = (torch.empty((fsplits, B, hq, hd), device=dev), torch.empty((fsplits, hq, B), device=dev))
-    plan = torch.zeros(2 + hkv, device=dev, dtype=torch.int32)
+    plan = torch.zeros(1, device=dev, dtype=torch.int32)
     one_launch = not kernels.far_read_uses_tcgen05(hd, B, hq, hkv)  # as FoldAttention chooses
     ws = (W + B - 1, B - 1)
 

@@ -89,8 +89,7 @@ class FoldWorkspace:
         self._parts = {}
         self._window_parts = {}
         self._step_far, self._step_window = {}, {}
-        # the step read's split (window blocks) and far-tile tickets per KV head
-        self.plan = torch.zeros(2 + hkv, device=cache.device, dtype=torch.int32)
+        self.plan = torch.zeros(1, device=cache.device, dtype=torch.int32)  # the step read's split
         if num_heads is not None:  # the buffers the forward of this layer uses, before any graph capture
             hq = int(num_heads)
             if mode != "window" and self.one_launch(self.block, hq):

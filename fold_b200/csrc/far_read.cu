@@ -22,44 +22,58 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarPa
   split_read<C, true>(nullptr, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
-// A window tile costs up to about this many far tiles (in tenths): the window read copies 16-byte
-// chunks with cp.async, which one SM issues at a lower rate than TMA moves the far read's boxes.
-// The estimate is on the high side on purpose: window blocks that finish early take far tiles.
-constexpr int kWindowTileCost10 = 40;
+// Cost model of the step read, in tenths of a far tile: a window tile (the window read copies
+// 16-byte chunks with cp.async, which one SM issues at a lower rate than TMA moves the far read's
+// boxes; measured at about 4 far tiles), and the second prologue and epilogue of a block that
+// reads both.
+constexpr int kWindowTileCost10 = 42;
+constexpr int kPhaseCost10 = 20;
 
-// How many of a KV head's S blocks read the window in this step, from the device-side lengths:
-// the fewest whose window share stays within 3/4 of a block's average work. Every block of the
-// launch computes the same count.
+// How a step's S blocks per KV head share the two reads, from the device-side lengths (every
+// block computes the same): w window blocks, the fewest whose window share (with a second
+// prologue) fits a block's average work, and `fw` far tiles for each of them after the window.
+struct StepSplit {
+  int w, fw, far_tiles;
+};
+
 template <class C>
-__device__ __forceinline__ int window_blocks(const FarParams& far, const FarParams& win, int S) {
+__device__ __forceinline__ StepSplit step_split(const FarParams& far, const FarParams& win, int S) {
   const int qlen = far.qsl[1] - far.qsl[0];
   const int seq = far.seq[0];
   const int hist = max(seq - qlen, 0);
   int64_t pos0, end;
-  const int64_t F = far_tiles<C::TK>(far, hist, &pos0, &end);
-  const int64_t Wt = window_tiles<C::TK>(win, hist, seq, &pos0, &end);
-  const int64_t total = 10 * F + kWindowTileCost10 * Wt;  // all work of the head, tenths of a far tile
-  for (int w = 1; w < S - 1; ++w)
-    if (4 * kWindowTileCost10 * ((Wt + w - 1) / w) * S <= 3 * total) return w;
-  return max(S - 1, 1);
+  const int F = far_tiles<C::TK>(far, hist, &pos0, &end);
+  const int Wt = window_tiles<C::TK>(win, hist, seq, &pos0, &end);
+  StepSplit sp{max(S - 1, 1), 0, F};
+  for (int w = 1; w < S; ++w) {
+    const int64_t avg = (10ll * F + static_cast<int64_t>(kWindowTileCost10) * Wt + kPhaseCost10 * w) / S;
+    const int64_t mine = static_cast<int64_t>(kWindowTileCost10) * ((Wt + w - 1) / w) + kPhaseCost10;
+    if (mine <= avg || w == S - 1) {
+      sp.w = w;
+      sp.fw = static_cast<int>(max64(avg - mine, 0) / 10);
+      if (static_cast<int64_t>(sp.fw) * w > F) sp.fw = F / w;
+      break;
+    }
+  }
+  return sp;
 }
 
 // The far read and the window read of one draft step in one launch. Of the S = gridDim.x blocks of
-// KV head blockIdx.y, the first w (window_blocks) read the window into window slots [0, w); then
-// every block reads far tiles, which the head's blocks draw in grants from a tile counter
-// (split_read<DYN>) until none are left, into far slot blockIdx.x. So the window read (a few MB)
-// runs beside the far read, and the blocks that read it take fewer far tiles. Block (0, 0)
-// stores w in plan[0] for the merge; plan[1] counts finished blocks and plan[2 + h] is head h's
-// tile counter: the last block to finish sets both back to zero for the next launch.
+// KV head blockIdx.y, the first w read their share of the window into window slots [0, w) and
+// then far tiles [x * fw, (x + 1) * fw); the other S - w blocks share the remaining far tiles
+// evenly. Every block writes far slot blockIdx.x (a block without far tiles writes an empty
+// partial). So the window read (a few MB) runs beside the far read, and its blocks take a smaller
+// share of the far tiles. Block (0, 0) stores w in plan[0] for the merge.
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     step_read_kernel(const __grid_constant__ CUtensorMap far_map, const FarParams far, const FarParams win,
                      int* plan) {
   const int S = static_cast<int>(gridDim.x), x = static_cast<int>(blockIdx.x), h = static_cast<int>(blockIdx.y);
-  const int w = window_blocks<C>(far, win, S);
-  if (x == 0 && h == 0 && threadIdx.x == 0) *plan = w;
-  if (x < w) {
-    split_read<C, true>(nullptr, nullptr, win, x, h, w);
+  const StepSplit sp = step_split<C>(far, win, S);
+  if (x == 0 && h == 0 && threadIdx.x == 0) *plan = sp.w;
+  int b0, b1;  // this block's far tiles
+  if (x < sp.w) {
+    split_read<C, true>(nullptr, nullptr, win, x, h, sp.w);
     // The window read is done: its stage barriers are re-initialised for the far read (every
     // phase is complete), and its generic shared-memory accesses are ordered before the far
     // read's TMA writes into the same stages.
@@ -68,17 +82,13 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     if (threadIdx.x == 0)
       for (int i = 0; i < C::NSTAGE; ++i) mbar_inval(stage_barriers<C>() + i);
     __syncthreads();
+    b0 = x * sp.fw, b1 = b0 + sp.fw;
+  } else {
+    const int base = min(sp.w * sp.fw, sp.far_tiles), rest = sp.far_tiles - base, j = x - sp.w, n = S - sp.w;
+    b0 = base + static_cast<int>(static_cast<int64_t>(rest) * j / n);
+    b1 = base + static_cast<int>(static_cast<int64_t>(rest) * (j + 1) / n);
   }
-  split_read<C, false, true>(&far_map, nullptr, far, x, h, S);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();  // this block's ticket draws, before it counts itself
-    const unsigned total = gridDim.x * gridDim.y;
-    if (static_cast<unsigned>(atomicAdd(plan + 1, 1)) == total - 1) {
-      for (unsigned i = 0; i < gridDim.y; ++i) atomicExch(plan + 2 + i, 0);
-      atomicExch(plan + 1, 0);
-    }
-  }
+  split_read<C, false>(&far_map, nullptr, far, x, h, S, b0, b1 - b0);
 }
 
 // ------------------------------------------------------------------ host side
@@ -340,7 +350,6 @@ int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_h
                 "step read: this shape's far read takes the tcgen05 kernel (fold_far_read_kernel_for); issue "
                 "fold_far_read and fold_window_read");
   if (splits < 2) return fail(FOLD_ERR_INVALID_ARGUMENT, "step read: at least 2 blocks per KV head");
-  far.tickets = plan + 2;
   return with_mma_config(hd, rows, StepLaunch{far, win, side, pages, plan, static_cast<cudaStream_t>(stream)});
 }
 

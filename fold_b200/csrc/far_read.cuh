@@ -39,12 +39,7 @@ struct FarParams {
   const int* block_table;
   int bt_len, num_blocks, block_size;
   int win_left, win_right, causal;
-  // Far read with tiles handed out per step (the step read): one counter per KV head of the tiles
-  // granted so far. Zero before a launch, zero after it.
-  int* tickets;
 };
-
-constexpr int kTicketTiles = 2;  // the smallest grant of tiles
 
 constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100
 

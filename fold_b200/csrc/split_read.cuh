@@ -289,26 +289,19 @@ __device__ __forceinline__ uint64_t* stage_barriers() {
 //   WIN = true, window read: K and V rows of the paged cache (p.kc, p.vc, cp.async by every
 //     thread), the query as given, row r reads its exact-position window
 //     (fold/attention.py:148-151,163).
-// DYN (far memory only): instead of the fixed range of split `split`, the CTA takes its tiles
-// from the head's tile counter (p.tickets[h]) in grants until the head's tiles are all taken;
-// `split` is then only the slot of its partial. A grant is the tiles left after the CTA's current
-// one divided by twice the CTA count (guided self-scheduling, at least kTicketTiles), so a CTA
-// draws a handful of grants, large ones first and small ones at the end. Thread 0 draws them one
-// grant ahead, so that the atomic's latency stays off the refill path, and records each stage's
-// tile in shared memory beside the stage's mbarrier; a stage marked -1 (completed by a plain
-// arrival) ends the loop for every warp.
-template <class C, bool WIN, bool DYN = false>
+// The CTA reads tiles [t_begin, t_begin + ntiles) of the cache's tiles for the step: the share of
+// split `split` of `nsplits`, or, with range_begin >= 0, the range [range_begin, range_begin +
+// range_tiles) clipped to the step's tiles (`split` is then only the slot of its partial).
+template <class C, bool WIN>
 __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
-                                           int split, int h, int nsplits) {
-  static_assert(!(WIN && DYN), "tiles by ticket are for the far read");
+                                           int split, int h, int nsplits, int range_begin = -1,
+                                           int range_tiles = 0) {
   constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
   constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  volatile int* st_tile = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * C::NSTAGE);  // DYN
-  static_assert(C::NSTAGE * 12 <= 64, "stage barriers and tiles share 64 bytes");
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_Q);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
   float* row_m = reinterpret_cast<float*>(smem + C::OFF_ROW);
@@ -330,41 +323,16 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   int64_t end;   // far: end of this cache's keys for the last row
   int64_t pos0;  // position of tile 0
   const int tiles = WIN ? window_tiles<TK>(p, hist, seq, &pos0, &end) : far_tiles<TK>(p, hist, &pos0, &end);
-  const int t_begin = static_cast<int>(static_cast<int64_t>(tiles) * split / nsplits);
-  const int ntiles = static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / nsplits) - t_begin;
+  const int t_begin = range_begin >= 0 ? min(range_begin, tiles)
+                                       : static_cast<int>(static_cast<int64_t>(tiles) * split / nsplits);
+  const int ntiles = range_begin >= 0
+                         ? max(min(range_begin + range_tiles, tiles) - t_begin, 0)
+                         : static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / nsplits) - t_begin;
 
   uint64_t pol = 0;
   // Window read: lane 0 of each warp holds the block of the warp's rows in the next tile to be
   // issued (looked up one tile ahead, so that the lookup's latency is off the refill's path).
   int next_blk = -1;
-  // DYN, thread 0: the tiles [cur_t, cur_end) left of the current grant, the grant drawn ahead
-  // (first tile and size), stages filled so far (markers included), and whether the end marker
-  // has been written.
-  int cur_t = 0, cur_end = 0, next_start = 0, next_take = 0, filled = 0;
-  bool exhausted = false;
-  auto grant_size = [&](int seen) { return max(kTicketTiles, (tiles - seen) / (2 * nsplits)); };
-  auto grab = [&]() -> int {  // the CTA's next tile, or -1 once the head's tiles are all taken
-    if (cur_t >= cur_end) {
-      cur_t = next_start;
-      cur_end = min(next_start + next_take, tiles);
-      if (cur_t >= tiles) return -1;
-      next_take = grant_size(cur_end);
-      next_start = atomicAdd(p.tickets + h, next_take);
-    }
-    return cur_t++;
-  };
-  // DYN, thread 0: fills stage st with the next tile, or with the end marker.
-  auto fill = [&](int st) {
-    const int t = grab();
-    st_tile[st] = t;
-    ++filled;
-    if (t < 0) {
-      exhausted = true;
-      mbar_arrive(&full[st]);
-    } else {
-      issue_tile<C>(smem, full, map, st, t, p.hkv, h, pol);
-    }
-  };
   // Tile t of this cache into stage st: far read by thread 0 (TMA), window read by every thread.
   auto issue = [&](int st, int t) {
     if constexpr (WIN) {
@@ -391,13 +359,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       // Fill the ring right away, so the first copies overlap the query rotation below.
       pol = l2_evict_first_policy();
       prefetch_tensormap(map);
-      if constexpr (DYN) {
-        next_take = grant_size(0);
-        next_start = atomicAdd(p.tickets + h, next_take);
-        for (int i = 0; i < NSTAGE && !exhausted; ++i) fill(i);
-      } else {
-        for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
-      }
+      for (int i = 0; i < NSTAGE && i < ntiles; ++i) issue(i, t_begin + i);
     }
   }
 
@@ -524,14 +486,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   int consumed = 0;
   const uint32_t p_base = smem_u32(smem + C::OFF_P);
 
-  for (int it = 0; DYN || it < ntiles; ++it) {
+  for (int it = 0; it < ntiles; ++it) {
     const int st = it % NSTAGE;
     const bool ok = mbar_wait(&full[st], (it / NSTAGE) & 1);
-    int tile = t_begin + it;  // this tile's index in the cache
-    if constexpr (DYN) {
-      tile = st_tile[st];  // written by thread 0 before it armed the stage
-      if (tile < 0) break;  // the end marker: the same stage, so the same decision, in every warp
-    }
+    const int tile = t_begin + it;  // this tile's index in the cache
     const uint32_t kv_base = smem_u32(smem + st * C::STAGE_BYTES);
     const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
     const int64_t tpos = pos0 + static_cast<int64_t>(tile) * TK;  // first position of the tile
@@ -618,11 +576,8 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     // One barrier per tile: P^T of every warp is written, every warp is done with the previous
     // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
     const bool attention = named_bar_or(exceed || !ok, 1, NTH);
-    if constexpr (DYN) {
-      if (tid == 0 && it >= 1 && !exhausted) fill((it - 1) % NSTAGE);
-    } else if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles) {
+    if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles)
       issue((it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE);
-    }
     if (attention) {
       if (named_bar_or(!ok, 2, NTH)) {
         timed_out = true;
@@ -739,7 +694,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     if constexpr (WIN) {
       cp_async_wait_all();
     } else if (tid == 0) {
-      const int issued = DYN ? filled : min(ntiles, max(consumed, 1) - 1 + NSTAGE);
+      const int issued = min(ntiles, max(consumed, 1) - 1 + NSTAGE);
       for (int i = consumed; i < issued; ++i)
         if (!mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1)) break;
     }

@@ -257,8 +257,8 @@ def step_read(q_far, q_win, qsl, seq_lens, side, far_parts, k_cache, v_cache, bl
     """The far read (as far_read, of q_far) and the window read (as window_read, of q_win) of one
     draft step in one launch: the S blocks of each KV head share the two reads, split per step
     from the device-side lengths. far_parts and window_parts are (o, lse) buffers of S slots each;
-    plan (int32 [2 + Hkv], device, zero before the first call) holds the step's split (window
-    blocks, read by merge_partials) and the far read's per-head tile tickets. The far softmax scale is alpha * softmax_scale, the window's softmax_scale. Not for
+    the step stores its split (window blocks) in plan (int32 [1], device), which merge_partials
+    reads. The far softmax scale is alpha * softmax_scale, the window's softmax_scale. Not for
     shapes whose far read takes the tcgen05 kernel (far_read_uses_tcgen05)."""
     (fo_, fl_), (wo_, wl_) = far_parts, window_parts
     _require_cuda(q_far, q_win, qsl, seq_lens, side, fo_, fl_, k_cache, v_cache, block_table, wo_, wl_, plan, table,
@@ -270,8 +270,8 @@ def step_read(q_far, q_win, qsl, seq_lens, side, far_parts, k_cache, v_cache, bl
     splits = _check_partials(fo_, fl_, n, hq, d, "step_read")
     if _check_partials(wo_, wl_, n, hq, d, "step_read") != splits:
         raise FoldError("step_read: the far and window partials must have the same number of slots")
-    if plan.dtype != torch.int32 or plan.numel() < 2 + side.shape[1] or not plan.is_contiguous():
-        raise FoldError("step_read: plan must be a contiguous int32 tensor of 2 + Hkv elements")
+    if plan.dtype != torch.int32 or plan.numel() < 1:
+        raise FoldError("step_read: plan must be an int32 tensor of at least one element")
     q_far, side_args = _side_args(q_far, side, table, rot_dim, pos_lo, capacity, far_len)
     q_win, paged = _paged_args(q_win, k_cache, v_cache, block_table, window_size, causal)
     _lib.call("fold_step_read", _p(q_far), q_far.stride(0), q_far.stride(1), _p(q_win), q_win.stride(0),

@@ -138,13 +138,12 @@ int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
  * (at least 2; fold_far_read_default_splits, one block per SM in all, keeps the launch one wave)
  * share the two reads: from the device-side lengths each step picks w, the number that read the
  * window, so that the window read (a few MB) runs beside the far read instead of after it. The
- * window read fills window slots [0, w); then every block draws far tiles from its KV head's
- * ticket counter until none are left, so the window blocks take fewer, and writes far slot
- * [its index] of partial sets of `splits` slots each. `plan` is a device array of 2 + hkv ints,
- * zero before the first call: the step stores w in plan[0], which fold_merge_partials reads;
- * plan[1] and plan[2 ..] are the step's block count and ticket counters, back to zero when the
- * step ends. Shapes whose far read takes the tcgen05 kernel (fold_far_read_kernel_for) fail with
- * FOLD_ERR_UNSUPPORTED: issue fold_far_read and fold_window_read for them. */
+ * window read fills window slots [0, w); the window blocks then read a smaller share of the far
+ * tiles than the others (a cost model of the two reads), and every block writes far slot [its
+ * index] of partial sets of `splits` slots each. The step stores w in plan[0] (a device int),
+ * which fold_merge_partials reads. Shapes whose far read takes the tcgen05 kernel
+ * (fold_far_read_kernel_for) fail with FOLD_ERR_UNSUPPORTED: issue fold_far_read and
+ * fold_window_read for them. */
 int fold_step_read(const void* q_far, int64_t qf_stride_tok, int64_t qf_stride_head, const void* q_win,
                    int64_t qw_stride_tok, int64_t qw_stride_head, const int* qsl, const int* seq_lens,
                    const float* rope_table, int table_rows, int rot_dim, const void* side, int pages, int64_t pos_lo,
@@ -188,7 +187,7 @@ int fold_merge(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, c
  * by fold_window_read) and the far read's fsplits partials (as written by fold_far_read) are each
  * combined by log-sum-exp, then merged with the alpha weighting of fold_merge. fsplits = 0 (far
  * pointers may then be NULL) writes the combined window read alone (the window ablation and plain
- * sliding layers). `plan` (may be NULL) is fold_step_read's plan array: then wsplits == fsplits
+ * sliding layers). `plan` (may be NULL) is fold_step_read's device word: then wsplits == fsplits
  * and the window set uses its first plan[0] slots, the far set all fsplits. All
  * partials float32 and contiguous; out bf16 with strides (tok, head). */
 int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplits, const float* o_fpart,
