@@ -330,6 +330,15 @@ def run_gpu(args):
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    align_buf = torch.zeros(1, device=dev)
+
+    def align():
+        """N > 1: a one-float all-reduce enqueued on the timing stream right before the start event,
+        so that every rank's timed region starts when the collective completes on the devices, not
+        when each host process gets past its barrier (host skew would count in the max over ranks)."""
+        if world > 1:
+            dist.all_reduce(align_buf)
+
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
@@ -370,6 +379,7 @@ def run_gpu(args):
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
+        align()
         e0.record(stream)
         timed_steps()
         e1.record(stream)
@@ -438,6 +448,7 @@ def run_gpu(args):
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
+        align()
         f0.record(stream)
         alt_graph.replay()
         f1.record(stream)
@@ -899,6 +910,8 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+            dist.all_reduce(torch.zeros(1, device=dev))  # device-aligned start (see align() above)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(compute)
         fn(args.warmup, total)

@@ -24,9 +24,8 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarPa
 
 // Cost model of the step read, in tenths of a far tile: a window tile (the window read copies
 // 16-byte chunks with cp.async, which one SM issues at a lower rate than TMA moves the far read's
-// boxes; measured at about 4 far tiles), and the second prologue and epilogue of a block that
-// reads both.
-constexpr int kWindowTileCost10 = 42;
+// boxes), and the second prologue and epilogue of a block that reads both.
+constexpr int kWindowTileCost10 = 30;
 constexpr int kPhaseCost10 = 20;
 
 // How a step's S blocks per KV head share the two reads, from the device-side lengths (every

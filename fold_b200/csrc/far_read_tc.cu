@@ -1,16 +1,19 @@
 // Far read on the fifth-generation tensor cores: tcgen05 MMAs with accumulators in tensor memory
 // (TMEM), operands staged in shared memory by TMA.
 //
-// One CTA per (split, KV head), 6 warps with fixed roles:
-//   warp 4 lane 0  TMA producer: streams 32 KB units (128 keys x 128 columns of K or of V) of this
+// One CTA per (split, KV head), 10 warps with fixed roles:
+//   warp 8 lane 0  TMA producer: streams 32 KB units (128 keys x 128 columns of K or of V) of this
 //                  head's side-cache rows into a ring of shared-memory slots;
-//   warp 5 lane 0  MMA issuer:   S^T(i) = K(i) . Q^T  into one of two TMEM buffers (M = 128 keys,
+//   warp 9 lane 0  MMA issuer:   S^T(i) = K(i) . Q^T  into one of two TMEM buffers (M = 128 keys,
 //                  N = the n*G query rows padded to 16..64), and O^T += V^T(i-1) . P^T(i-1)
 //                  (M = 128 head dims per block, accumulated in TMEM across the whole split);
-//   warps 0-3      softmax: thread t owns key t of the tile (TMEM lane t), loads its S^T row,
-//                  masks, raises the row maxima lazily (as in the mma.sync kernel), writes P^T
-//                  to shared memory and keeps per-thread row sums; at the end they read O^T and
-//                  write the split's normalised partial.
+//   warps 0-7      softmax: warp w reads TMEM lane quarter w % 4 (a thread owns one key of the
+//                  tile) and column half w / 4 of S^T, masks, raises the row maxima lazily (as in
+//                  the mma.sync kernel), writes its part of P^T to shared memory and keeps
+//                  per-thread row sums; at the end they read O^T and write the split's
+//                  normalised partial. With four softmax warps (all columns per thread, one warp
+//                  per SM sub-partition) the softmax bounded the kernel: 112.7 us at the 128K
+//                  Llama shape against 97.8 us for the mma.sync kernel (ncu, same box).
 // Shared-memory operand layouts (sm_100 matrix descriptors):
 //   K tile   K-major, 128-byte swizzle: exactly what TMA writes (64-column boxes of 128 B rows);
 //   Q        K-major, 128-byte swizzle, written by the rotation prologue;
@@ -72,15 +75,40 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-// N (16..64, multiple of 16) consecutive columns with one wait for all of them.
+// 8 consecutive 32-bit TMEM columns of this thread's lane, waited for.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// N (8, 16, 24 or 32) consecutive columns with one wait for all of them.
 template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
-  static_assert(N % 16 == 0 && N <= 64, "columns");
-  uint32_t r[64];
-  if constexpr (N == 16) {
+  static_assert(N == 8 || N == 16 || N == 24 || N == 32, "columns");
+  uint32_t r[32];
+  if constexpr (N == 8) {
+    tmem_ld8(taddr, v);
+    return;
+  } else if constexpr (N == 16) {
     tmem_ld16(taddr, v);
     return;
-  } else if constexpr (N == 32) {
+  } else if constexpr (N == 24) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%24];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%25];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23])
+        : "r"(taddr), "r"(taddr + 16)
+        : "memory");
+  } else {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
@@ -91,52 +119,17 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr)
         : "memory");
-  } else if constexpr (N == 48) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%48];\n\t"
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47},"
-        " [%49];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
-        : "r"(taddr), "r"(taddr + 32)
-        : "memory");
-  } else {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-        : "r"(taddr)
-        : "memory");
   }
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n\t"
       "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
       "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
       : "memory");
 }
 
@@ -187,14 +180,18 @@ struct TcCfg {
   static constexpr int UPT = 2 * KU;   // units per tile
   static constexpr int BOX_BYTES = TK * 128;
   static constexpr int UNIT_BYTES = 2 * BOX_BYTES;
-  static constexpr int NSW = 4;  // softmax warps
+  // Softmax warps: warp w serves TMEM lane quarter w % 4 (keys of the tile; head dims of O^T)
+  // and column half w / 4 (query rows [HALF * (w / 4), HALF * (w / 4 + 1))), so two warps share
+  // every quarter of the lanes and each thread handles half of a key's columns.
+  static constexpr int NSW = 8;
   static constexpr int NSM = NSW * 32;
   static constexpr int NTHREADS = NSM + 64;
+  static constexpr int HALF = NP / 2;
   static constexpr int Q_CHUNK = NP * 128;  // 64 columns of Q, swizzled
   static constexpr int Q_BYTES = (HD / 64) * Q_CHUNK;
   static constexpr int P_HALF = NP * TK * 2;  // one bf16 part of P^T
   static constexpr int P_BYTES = 2 * P_HALF;   // high and low parts
-  static constexpr int RED_BYTES = NSW * NP * 4;
+  static constexpr int RED_BYTES = 4 * NP * 4;  // [lane quarter][column]
   static constexpr int ROW_BYTES = 3 * NP * 4;  // row limits, row maxima, rescale factors
   static constexpr int NBAR = 26;
   static constexpr int BASE_FIXED = Q_BYTES + RED_BYTES + ROW_BYTES + NBAR * 8 + 16 + 1024;
@@ -216,6 +213,7 @@ struct TcCfg {
   static constexpr int TMEM_NEED = KU * NP + 2 * NP;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128 : 256;
   static_assert(NP % 16 == 0 && NP >= 16 && NP <= 64, "N of an M=128 MMA: multiple of 16");
+  static_assert(HALF % 8 == 0, "a column half is whole groups of 8 rows");
   static_assert(NSLOT >= UPT, "a tile's units must fit the ring");
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
   static_assert(TMEM_NEED <= 256, "TMEM columns");
@@ -510,10 +508,13 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     __syncwarp();
   } else {
     // -------------------------------------------------------------- softmax warps
-    float l[NP];  // this thread's share of the row sums
+    constexpr int HALF = C::HALF;
+    const int q4 = warp & 3, c_lo = (warp >> 2) * HALF;  // lane quarter and first column of this warp
+    const int lrow = q4 * 32 + lane;                      // this thread's TMEM lane
+    float l[HALF];  // this thread's share of the row sums of its columns
 #pragma unroll
-    for (int c = 0; c < NP; ++c) l[c] = 0.f;
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    for (int c = 0; c < HALF; ++c) l[c] = 0.f;
+    const uint32_t lane_addr = static_cast<uint32_t>(q4 * 32) << 16;
     const uint32_t p_base_gen = C::OFF_P;
     bool timed_out = false;
     bool bad = false;  // a wait of this thread gave up; acted on uniformly at the next barrier
@@ -523,28 +524,28 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
       const int b = i & 1;
       // tcgen05.ld is warp-collective: the warp takes the tile only if every lane saw it land
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (i >> 1) & 1));
-      float x[NP];
+      float x[HALF];
       if (ok) {
         tc_fence_after();
-        tmem_ld_cols<NP>(tmem + C::TMEM_S + b * NP + lane_addr, x);
+        tmem_ld_cols<HALF>(tmem + C::TMEM_S + b * NP + c_lo + lane_addr, x);
       } else {
 #pragma unroll
-        for (int c = 0; c < NP; ++c) x[c] = -INFINITY;
+        for (int c = 0; c < HALF; ++c) x[c] = -INFINITY;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);
 
       const int64_t key0 = p.pos_lo + static_cast<int64_t>(t_begin + i) * TK;
-      const int64_t key = key0 + tid;
+      const int64_t key = key0 + lrow;
       const bool clean = key0 + TK <= lim_lo;  // every key of the tile is valid for every row
       bool exceed = i == 0;  // the first tile always sets the row maxima
 #pragma unroll
-      for (int c = 0; c < NP; ++c) {
+      for (int c = 0; c < HALF; ++c) {
         float v = x[c] * p.scale_log2;
-        if (!clean && key >= lims[c]) v = -INFINITY;
+        if (!clean && key >= lims[c_lo + c]) v = -INFINITY;
         x[c] = v;
-        exceed |= v > rowm[c] + kRaise;
+        exceed |= v > rowm[c_lo + c] + kRaise;
       }
       if (named_bar_or(exceed || !ok || bad, 1, NSM)) {
         if (named_bar_or(!ok || bad, 2, NSM)) {
@@ -554,11 +555,11 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
         }
         // ---- raise the row maxima that a logit passed by more than kRaise
 #pragma unroll
-        for (int c = 0; c < NP; ++c) {
+        for (int c = 0; c < HALF; ++c) {
           float v = x[c];
 #pragma unroll
           for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-          if (lane == 0) red[warp * NP + c] = v;
+          if (lane == 0) red[q4 * NP + c_lo + c] = v;
         }
         named_bar_sync(2, NSM);
         if (tid < NP) {  // thread c owns row maximum c
@@ -570,7 +571,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
         }
         named_bar_sync(2, NSM);  // new maxima and factors visible; red free again
 #pragma unroll
-        for (int c = 0; c < NP; ++c) l[c] *= rowf[c];
+        for (int c = 0; c < HALF; ++c) l[c] *= rowf[c_lo + c];
         if (i >= 1) {
           // O^T holds the PV products up to tile i-1: let them finish, then scale its columns
           if (!mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1)) bad = true;
@@ -578,31 +579,32 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
 #pragma unroll
           for (int hh = 0; hh < KU; ++hh) {
 #pragma unroll
-            for (int c0 = 0; c0 < NP; c0 += 16) {
-              float v[16];
-              const uint32_t a = tmem + C::TMEM_O + hh * NP + c0 + lane_addr;
-              tmem_ld16(a, v);
+            for (int c0 = 0; c0 < HALF; c0 += 8) {
+              float v[8];
+              const uint32_t a = tmem + C::TMEM_O + hh * NP + c_lo + c0 + lane_addr;
+              tmem_ld8(a, v);
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] *= rowf[c0 + j];
-              tmem_st16(a, v);
+              for (int j = 0; j < 8; ++j) v[j] *= rowf[c_lo + c0 + j];
+              tmem_st8(a, v);
             }
           }
         }
       }
-      // ---- P^T of this thread's key: 16-byte stores into [row group][key][8 rows]
+      // ---- P^T of this thread's key and columns: 16-byte stores into [row group][key][8 rows],
+      // the high bf16 part and the rest in the buffer's two halves
       if (i >= C::P_BUFS) {  // the PV MMAs of tile i - P_BUFS read this buffer
         const int t = i - C::P_BUFS;
         if (!mbar_wait(&pv_done[t & 1], (t >> 1) & 1)) bad = true;
       }
-      unsigned char* pb = smem + p_base_gen + (i % C::P_BUFS) * C::P_BYTES + tid * 16;
+      unsigned char* pb = smem + p_base_gen + (i % C::P_BUFS) * C::P_BYTES + (c_lo / 8) * TK * 16 + lrow * 16;
 #pragma unroll
-      for (int g = 0; g < NP / 8; ++g) {
+      for (int g = 0; g < HALF / 8; ++g) {
         uint32_t w[4], wl[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = g * 8 + 2 * j;
-          const float m0 = rowm[c] == -INFINITY ? 0.f : rowm[c];
-          const float m1 = rowm[c + 1] == -INFINITY ? 0.f : rowm[c + 1];
+          const float m0 = rowm[c_lo + c] == -INFINITY ? 0.f : rowm[c_lo + c];
+          const float m1 = rowm[c_lo + c + 1] == -INFINITY ? 0.f : rowm[c_lo + c + 1];
           const float p0 = fast_exp2(x[c] - m0), p1 = fast_exp2(x[c + 1] - m1);
           w[j] = pack_bf16(p0, p1);  // high parts
           const float h0 = __uint_as_float(w[j] << 16), h1 = __uint_as_float(w[j] & 0xffff0000u);
@@ -626,11 +628,11 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     // -------------------------------------------------------------- epilogue
     // row sums over the 128 keys of each tile position
 #pragma unroll
-    for (int c = 0; c < NP; ++c) {
+    for (int c = 0; c < HALF; ++c) {
       float v = l[c];
 #pragma unroll
       for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) red[warp * NP + c] = v;
+      if (lane == 0) red[q4 * NP + c_lo + c] = v;
     }
     named_bar_sync(2, NSM);
     const bool landed = ntiles == 0 || mbar_wait(o_final, 0);
@@ -650,25 +652,26 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
             live ? (rowm[tid] + __log2f(L)) * kLn2 : -INFINITY;
     }
     named_bar_sync(2, NSM);
-    float inv[NP];
-    int off[NP];
+    float inv[HALF];
+    int off[HALF];
 #pragma unroll
-    for (int c = 0; c < NP; ++c) inv[c] = row_inv[c], off[c] = row_off[c];
+    for (int c = 0; c < HALF; ++c) inv[c] = row_inv[c_lo + c], off[c] = row_off[c_lo + c];
     tc_fence_after();
-    float* __restrict__ out = p.o_part + static_cast<int64_t>(split) * p.n * p.hq * HD + tid;
+    // O^T lane = head dim: this thread writes head dim lrow of its rows
+    float* __restrict__ out = p.o_part + static_cast<int64_t>(split) * p.n * p.hq * HD + lrow;
 #pragma unroll
     for (int hh = 0; hh < KU; ++hh) {
 #pragma unroll
-      for (int c0 = 0; c0 < NP; c0 += 16) {
-        float v[16];
+      for (int c0 = 0; c0 < HALF; c0 += 8) {
+        float v[8];
         if (fin && ntiles > 0) {
-          tmem_ld16(tmem + C::TMEM_O + hh * NP + c0 + lane_addr, v);
+          tmem_ld8(tmem + C::TMEM_O + hh * NP + c_lo + c0 + lane_addr, v);
         } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (int j = 0; j < 8; ++j) v[j] = 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < 8; ++j)
           if (off[c0 + j] >= 0) out[off[c0 + j] + hh * 128] = v[j] * inv[c0 + j];
       }
     }
