@@ -150,14 +150,6 @@ __device__ __forceinline__ uint32_t pack_f16_sat(float lo, float hi) {
   asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-// The two f16 halves of a packed pair as floats (low half first).
-__device__ __forceinline__ float2 unpack_f16(uint32_t x) {
-  float2 v;
-  asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
-      : "=f"(v.x), "=f"(v.y)
-      : "r"(x));
-  return v;
-}
 // A packed bf16 pair re-encoded as an f16 pair (exact in the f16 normal range; magnitudes past it
 // saturate at +-65504, values below it become f16 subnormals or zero).
 __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {

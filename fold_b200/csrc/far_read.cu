@@ -25,8 +25,8 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarPa
 // Cost model of the step read, in tenths of a far tile: a window tile (the window read copies
 // 16-byte chunks with cp.async, which one SM issues at a lower rate than TMA moves the far read's
 // boxes), and the second prologue and epilogue of a block that reads both.
-constexpr int kWindowTileCost10 = 30;
-constexpr int kPhaseCost10 = 20;
+constexpr int kWindowTileCost10 = 24;
+constexpr int kPhaseCost10 = 30;
 
 // How a step's S blocks per KV head share the two reads, from the device-side lengths (every
 // block computes the same): w window blocks, the fewest whose window share (with a second

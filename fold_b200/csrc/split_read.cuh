@@ -21,10 +21,9 @@
 // the fp32 sums of at most 2^15 * (keys per split) stay far from overflow, so a high threshold
 // costs no accuracy and makes raises rare after the first tile.
 //
-// P is rounded to f16 (11 significant bits) for the PV product, and the row sums add the rounded
-// values, so the weights that multiply V sum to exactly the normaliser. With bf16 P (8 bits), a
-// row whose mass sits on a few keys carried the rounding of those weights straight into the
-// output: 0.03-0.05 on the x8 outlier channels of the 128K Llama workload. V tiles are bf16 in
+// P is rounded to f16 (11 significant bits) for the PV product. With bf16 P (8 bits), a row whose
+// mass sits on a few keys carried the rounding of those weights straight into the output:
+// 0.03-0.05 on the x8 outlier channels of the 128K Llama workload, against 0.002 with f16. V tiles are bf16 in
 // memory; their MMA fragments are re-encoded as f16 in registers (exact in the f16 range; the
 // conversion saturates at +-65504), since an MMA takes both operands in one type. Q and K stay
 // bf16 for S^T = K . Q^T.
@@ -558,11 +557,11 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         for (int j = 0; j < QNT; ++j) {
           const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
           const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-          const uint32_t pa = pack_f16_sat(fast_exp2(x[j][0] - m0), fast_exp2(x[j][1] - m1));
-          const uint32_t pb = pack_f16_sat(fast_exp2(x[j][2] - m0), fast_exp2(x[j][3] - m1));
-          const float2 ra = unpack_f16(pa), rb = unpack_f16(pb);
-          ls[j][0] = ra.x + rb.x;
-          ls[j][1] = ra.y + rb.y;
+          const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+          const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+          const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
+          ls[j][0] = p0 + p2;
+          ls[j][1] = p1 + p3;
           if (nt_lo + j < NT) {
             const int r0 = (nt_lo + j) * 8 + t4 * 2;
             const int k0 = mt * 16 + g4;
@@ -636,11 +635,11 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         }
         const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
         const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-        const uint32_t pa = pack_f16_sat(fast_exp2(x[j][0] - m0), fast_exp2(x[j][1] - m1));
-        const uint32_t pb = pack_f16_sat(fast_exp2(x[j][2] - m0), fast_exp2(x[j][3] - m1));
-        const float2 ra = unpack_f16(pa), rb = unpack_f16(pb);
-        ls[j][0] = ra.x + rb.x;
-        ls[j][1] = ra.y + rb.y;
+        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
+        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
+        const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
+        ls[j][0] = p0 + p2;
+        ls[j][1] = p1 + p3;
         if (nt_lo + j < NT) {
           const int r0 = (nt_lo + j) * 8 + t4 * 2;
           const int k0 = mt * 16 + g4;
