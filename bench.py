@@ -59,6 +59,7 @@ def parse():
                     help="fold: this library; reference: the CPU implementation of the path; fa4: the "
                          "reference's own GPU path (its Triton rotation and merge with FlashAttention-4) alone")
     ap.add_argument("--no-fa4", action="store_true", help="skip timing the reference's GPU path beside the step")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the leg with the fp8 side cache")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0, help="far-read splits per KV head (0: one CTA per SM)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -457,6 +458,10 @@ def run_gpu(args):
         del alt_graph
     window = run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err,
                         append) if world == 1 else None
+    fp8 = None
+    if world == 1 and args.impl == "fold" and not args.no_fp8:
+        fp8 = run_fp8(args, cfg, dev, stream, side, H, acc, q_all, seq_all, qsl, new_k, new_v, new_pos, o_l, lse_l,
+                      out, table, length, splits, err)
     fa4 = None
     if world == 1 and (args.impl == "fa4" or not args.no_fa4):
         fa4 = run_fa4(args, cfg, dev, stream, side, q_all, seq_all, qsl, new_k, new_v, new_pos, acc, o_l, lse_l,
@@ -532,6 +537,8 @@ def run_gpu(args):
         }
         if window is not None:
             line["window_read"] = window
+        if fp8 is not None:
+            line["fp8_side_cache"] = fp8
         if fa4 is not None:
             line["reference_gpu_path"] = fa4
         if args.impl == "fa4":  # the reference's GPU path as its own line
@@ -658,6 +665,89 @@ def run_fa4(args, cfg, dev, stream, side, q_all, seq_all, qsl, new_k, new_v, new
                     "(vllm.vllm_flash_attn, fa_version=4) + Triton merge, unmodified from baseline/_ref",
             "timing": "one CUDA graph of K steps after 0.3 s of back-to-back replays (sustained), CUDA events; "
                       "the far read alone likewise, burst and sustained"}
+
+
+def run_fp8(args, cfg, dev, stream, side, H, acc, q_all, seq_all, qsl, new_k, new_v, new_pos, o_l, lse_l, out,
+            table, length, splits, err):
+    """The same steps with the fp8 side cache (FoldWorkspace side_format "fp8"): the bf16 side
+    cache is quantised into it once (per-KV-head scales amax / 448), then each step appends the
+    accepted tokens with fold_append_fp8, reads the far memory with fold_far_read_fp8 and merges.
+    Timed like the headline step (one CUDA graph of K steps after 0.3 s of load); the far read
+    alone likewise, burst and sustained."""
+    import torch
+
+    from fold_b200 import kernels
+
+    hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
+    if hd != kernels.FP8_HEAD_DIM:
+        return None
+    pages = side.shape[0]
+    side8 = torch.zeros(kernels.fp8_side_shape(pages, hkv), device=dev, dtype=torch.uint8)
+    ks = (side[..., :hd].abs().amax(dim=(0, 2, 3)).float() / 448.0).contiguous()
+    vs = (side[..., hd:].abs().amax(dim=(0, 2, 3)).float() / 448.0).contiguous()
+    for a in range(0, (pages - 1) * 256, 16384):
+        pos = torch.arange(a, min(a + 16384, (pages - 1) * 256), device=dev)
+        k, v = kernels.gather(side, pos)
+        kernels.append_fp8(k, v, pos, pos, side8, ks, vs)
+    o_part = torch.empty((splits, B, hq, hd), device=dev, dtype=torch.float32)
+    lse_part = torch.empty((splits, hq, B), device=dev, dtype=torch.float32)
+    scale = hd ** -0.5 * ALPHA
+
+    def far(i):
+        kernels.far_read_fp8(q_all[i], qsl, seq_all[i: i + 1], side8, ks, vs, o_part, lse_part, window=W, block=B,
+                             far_distance=W + B, softmax_scale=scale, table=table, capacity=length, err=err)
+
+    def step(i):
+        a = int(acc[i - 1]) if i > 0 else 0
+        if a:
+            kernels.append_fp8(new_k[i - 1, :a], new_v[i - 1, :a], new_pos[i - 1, :a], new_pos[i - 1, :a], side8, ks,
+                               vs, err=err)
+        far(i)
+        kernels.merge(o_l, lse_l, o_part, lse_part, out, qsl, seq_all[i: i + 1], window=W, block=B, alpha=ALPHA)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def graph_of(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for j in range(args.steps):
+                fn(args.warmup + j)
+        g.replay()
+        torch.cuda.synchronize()
+        return g
+
+    def timed(g, sustained):
+        if sustained:
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < 0.3:
+                g.replay()
+                torch.cuda.synchronize()
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return 1000.0 * e0.elapsed_time(e1) / args.steps
+
+    gf = graph_of(far)
+    burst, sustained = timed(gf, False), timed(gf, True)
+    del gf
+    gs = graph_of(step)
+    us = timed(gs, True)
+    del gs
+    far_keys = statistics.mean(max(min(int(H[args.warmup + j]) - W, length), 0) for j in range(args.steps))
+    alg = far_keys * hkv * 2 * hd + B * hq * hd * 2 + splits * (B * hq * hd + hq * B) * 4
+    hbm_peak, peak_kind = peaks()
+    return {"us_per_step": round(us, 3), "unit": "us/draft-step", "far_read_us_sustained": round(sustained, 3),
+            "far_read_us_burst": round(burst, 3), "algorithmic_bytes": int(alg),
+            "achieved_gbs": round(alg / (sustained * 1e-6) / 1e9, 1), "peak": hbm_peak, "peak_kind": peak_kind,
+            "frac": round(alg / (sustained * 1e-6) / 1e9 / hbm_peak, 4),
+            "side_cache_bytes": int(side8.numel()), "kernel": "far_read_kernel<FarCfg<128, nt, 128, 4, fp8>>",
+            "how": "append_fp8 + far_read_fp8 + merge of the same steps, e4m3 K and V^T with per-KV-head scales "
+                   "(amax / 448); one CUDA graph of K steps after 0.3 s of load (sustained); far read alone burst "
+                   "and sustained"}
 
 
 def run_window(args, cfg, dev, stream, H, q_all, seq_all, qsl, side, table, pos_lo, out, length, err, append):

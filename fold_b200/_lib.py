@@ -23,6 +23,10 @@ SIGNATURES = {
     "fold_num_sms": [],
     "fold_append": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i64, _i32, _vp, _vp],
     "fold_gather": [_vp, _i32, _i32, _i32, _i64, _vp, _i32, _vp, _vp, _vp, _vp],
+    "fold_append_fp8": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _vp, _i64,
+                        _i32, _vp, _vp],
+    "fold_far_read_fp8": [_vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp,
+                          _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp],
     "fold_far_query": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i32, _i32, _i32,
                        _i32, _i32, _vp, _vp],
     "fold_rerope_query": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32,

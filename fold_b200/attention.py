@@ -48,14 +48,17 @@ class FoldWorkspace:
     side[pages, Hkv, 256, 2 * head_dim] with pages = ceil(max_model_len / 256) + 1, the last page
     holding the dummy slot. Extra keyword arguments: num_heads (query heads, to size the partials
     up front; else they are sized on first use), splits (far-read splits; default one CTA per SM),
-    and a shard of a sequence-partitioned cache (pos_lo = first position held, shard_len =
-    positions held)."""
+    a shard of a sequence-partitioned cache (pos_lo = first position held, shard_len = positions
+    held), and the storage format of the side cache: side_format "bf16" (the reference's, the
+    cache dtype) or "fp8" (e4m3 K and V^T at half the bytes per key, head size 128; k_scale and
+    v_scale are the per-KV-head dequantisation scales, a float or one per head: a stored value
+    is round(x / scale))."""
 
     side_block = kernels.SIDE_BLOCK
 
     def __init__(self, cache, window, block, max_model_len, *, inv_freq, far_distance, alpha=2.0, mode="fold",
                  logn_ref=0, num_heads: Optional[int] = None, splits: Optional[int] = None, pos_lo: int = 0,
-                 shard_len: Optional[int] = None):
+                 shard_len: Optional[int] = None, side_format: str = "bf16", k_scale=1.0, v_scale=1.0):
         if window < 1 or block < 1:
             raise FoldError("window and block size must be positive")
         if cache.ndim != 4 or cache.shape[-1] % 2:
@@ -66,6 +69,10 @@ class FoldWorkspace:
             raise FoldError(f"mode must be one of {MODES}")
         if pos_lo % self.side_block:
             raise FoldError("a shard must start on a side-cache page boundary")
+        if side_format not in ("bf16", "fp8"):
+            raise FoldError('side_format must be "bf16" or "fp8"')
+        if side_format == "fp8" and cache.shape[-1] != 2 * kernels.FP8_HEAD_DIM:
+            raise FoldError("the fp8 side cache needs head size 128")
         self.window, self.block, self.max_model_len = int(window), int(block), int(max_model_len)
         self.mode, self.alpha, self.logn_ref = mode, float(alpha), int(logn_ref)
         _, hkv, _, d2 = cache.shape
@@ -77,7 +84,13 @@ class FoldWorkspace:
         # the window ablation keeps no memory; one page beyond the held range holds the dummy slot
         pages = 1 if mode == "window" else (max(held, 0) + self.side_block - 1) // self.side_block + 1
         self.side_pages = pages
-        self.side = torch.zeros((pages, hkv, self.side_block, d2), device=cache.device, dtype=cache.dtype)
+        self.side_format = side_format
+        if side_format == "fp8":
+            self.side = torch.zeros(kernels.fp8_side_shape(pages, hkv), device=cache.device, dtype=torch.uint8)
+            self.k_scale, self.v_scale = (torch.as_tensor(x, dtype=torch.float32).to(cache.device).expand(hkv)
+                                          .contiguous() for x in (k_scale, v_scale))
+        else:
+            self.side = torch.zeros((pages, hkv, self.side_block, d2), device=cache.device, dtype=cache.dtype)
         self.side_table = torch.arange(pages, device=cache.device, dtype=torch.int32)[None]
         self.far_len = torch.zeros(1, device=cache.device, dtype=torch.int32)
         self.err = torch.zeros(1, device=cache.device, dtype=torch.int32)
@@ -136,7 +149,8 @@ class FoldWorkspace:
     def one_launch(self, n: int, num_heads: int) -> bool:
         """Whether the far and window reads of a step of n rows run as one launch (read_step): for
         an unsharded cache whose far read takes the mma.sync kernel."""
-        return not self.sharded and not kernels.far_read_uses_tcgen05(self.head_dim, n, num_heads, self.num_kv_heads)
+        return (not self.sharded and self.side_format == "bf16"
+                and not kernels.far_read_uses_tcgen05(self.head_dim, n, num_heads, self.num_kv_heads))
 
     def step_partials(self, n: int, num_heads: int):
         """(far, window) split buffers of the one-launch step read: splits() slots each (the
@@ -156,6 +170,10 @@ class FoldWorkspace:
     # -- the two kernels of a step ----------------------------------------------------------------
     def append(self, k, v, positions, slots):
         """Side-cache append of committed entries (keys before RoPE)."""
+        if self.side_format == "fp8":
+            kernels.append_fp8(k, v, positions, slots, self.side, self.k_scale, self.v_scale, pos_lo=self.pos_lo,
+                               skip_foreign=self.sharded, err=self.err)
+            return
         kernels.append(k, v, positions, slots, self.side, pos_lo=self.pos_lo, skip_foreign=self.sharded,
                        err=self.err)
 
@@ -163,6 +181,12 @@ class FoldWorkspace:
         """Rotated far read of q [n, Hq, D]; returns the partials (o [S, n, Hq, D], lse [S, Hq, n])."""
         n, hq, _ = q.shape
         o_part, lse_part = self.partials(n, hq)
+        if self.side_format == "fp8":
+            kernels.far_read_fp8(q, qsl, seq_lens, self.side, self.k_scale, self.v_scale, o_part, lse_part,
+                                 window=self.window, block=self.block, far_distance=self.far_distance,
+                                 softmax_scale=scale * self.alpha, table=self.table if rotate else None,
+                                 far_len=self.far_len, pos_lo=self.pos_lo, capacity=self.capacity, err=self.err)
+            return o_part, lse_part
         kernels.far_read(q, qsl, seq_lens, self.side, o_part, lse_part, window=self.window, block=self.block,
                          far_distance=self.far_distance, softmax_scale=scale * self.alpha,
                          table=self.table if rotate else None, far_len=self.far_len, pos_lo=self.pos_lo,

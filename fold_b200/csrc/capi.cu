@@ -93,6 +93,37 @@ int side_tensor_map(const void* side, int pages, int hkv, int hd, int box_rows, 
   return FOLD_OK;
 }
 
+int fp8_side_tensor_map(const void* side8, int pages, int hkv, CUtensorMap* out) {
+  int dev = 0;
+  if (int s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return s;
+  // hd -1 marks the fp8 layout in the cache key
+  MapKey key{reinterpret_cast<uintptr_t>(side8), pages, hkv, -1, 128, dev};
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return FOLD_OK;
+  }
+  if (int s = load_encode()) return s;
+  if (!aligned16(side8)) return fail(FOLD_ERR_ALIGNMENT, "fp8 side cache pointer is not 16-byte aligned");
+  // [pages][hkv][2 planes][2 halves][128 rows] rows of 128 bytes; one box = one 16 KB block
+  const cuuint64_t dims[2] = {128u, static_cast<cuuint64_t>(pages) * static_cast<cuuint64_t>(hkv) * 512u};
+  const cuuint64_t strides[1] = {128u};
+  const cuuint32_t box[2] = {128u, 128u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUtensorMap m;
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(side8), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FOLD_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled (fp8 side cache) failed with CUresult " +
+                                         std::to_string(r));
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return FOLD_OK;
+}
+
 int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out) {
   {
     std::lock_guard<std::mutex> lock(g_map_mutex);

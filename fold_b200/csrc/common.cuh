@@ -90,6 +90,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
       : "memory");
 }
+// 2-D tiled load global -> shared, completion counted in bytes on `bar` (c0 * element size a
+// multiple of 16 bytes).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
 // 16-byte asynchronous copy global -> shared through L2 (cp.async.cg); the bytes past src_bytes
 // (all 16 when src_bytes is 0) are zero-filled, and src is not read beyond src_bytes.
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -149,6 +159,14 @@ __device__ __forceinline__ uint32_t pack_f16_sat(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+// Four e4m3 bytes (little-endian order) as two f16 pairs: bytes 0-1 into `lo`, bytes 2-3 into
+// `hi` (every e4m3 value is exact in f16).
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t x, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(x));
 }
 // A packed bf16 pair re-encoded as an f16 pair (exact in the f16 normal range; magnitudes past it
 // saturate at +-65504, values below it become f16 subnormals or zero).

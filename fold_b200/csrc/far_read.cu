@@ -210,8 +210,12 @@ struct FarLaunch {
   template <class C>
   int run() const {
     CUtensorMap map;
-    const int s = cached_map ? side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)
-                             : side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map);
+    int s;
+    if constexpr (C::FP8)
+      s = fp8_side_tensor_map(side, pages, prm.hkv, &map);
+    else
+      s = cached_map ? side_tensor_map(side, pages, prm.hkv, C::HD, C::TK, &map)
+                     : side_tensor_map_uncached(side, pages, prm.hkv, C::HD, C::TK, &map);
     if (s) return s;
     static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(far_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(far_read)")) return e;
@@ -304,6 +308,26 @@ int fold_far_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (far_read_variant(hd, rows) == 1) return far_read_tc_launch(prm, side, pages, hd, ((rows + 15) / 16) * 16, true, st);
   return with_mma_config(hd, rows, FarLaunch{prm, side, pages, true, st});
+}
+
+int fold_far_read_fp8(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                      const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side8,
+                      int pages, int64_t pos_lo, int64_t capacity, int* far_len, const float* k_scale,
+                      const float* v_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
+                      int window, int block, int far_distance, float softmax_scale, int* err, void* stream) {
+  using namespace fold;
+  if (!k_scale || !v_scale) return fail(FOLD_ERR_INVALID_ARGUMENT, "fp8 far read: null scales");
+  if (hd != 128) return fail(FOLD_ERR_UNSUPPORTED, "fp8 far read: head size must be 128");
+  FarParams prm;
+  if (int s = make_far_params(q, q_stride_tok, q_stride_head, qsl, seq_lens, rope_table, table_rows, rot_dim, side8,
+                              pages, pos_lo, capacity, far_len, nullptr, 0, 0, o_part, lse_part, splits, n, hq, hkv,
+                              hd, window, block, far_distance, softmax_scale, err, &prm))
+    return s;
+  if (static_cast<int64_t>(pages) * hkv * 512 > (1ll << 31) - 1)
+    return fail(FOLD_ERR_INVALID_ARGUMENT, "fp8 far read: side cache too large for one descriptor");
+  prm.k_scale = k_scale, prm.v_scale = v_scale;
+  const FarLaunch f{prm, side8, pages, true, static_cast<cudaStream_t>(stream)};
+  return with_row_tiles<128, 128, 4, FarLaunch, true>((n * (hq / hkv) + 7) / 8, f);
 }
 
 int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl, const int* seq_lens,

@@ -39,6 +39,9 @@ struct FarParams {
   const int* block_table;
   int bt_len, num_blocks, block_size;
   int win_left, win_right, causal;
+  // Far read of an fp8 side cache only: per-KV-head dequantisation scales of K and V (float [hkv]).
+  const float* k_scale;
+  const float* v_scale;
 };
 
 constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA on sm_100

@@ -30,6 +30,10 @@ int side_tensor_map(const void* side, int pages, int hkv, int hd, int box_rows, 
 // The same descriptor, encoded into *out on every call without touching the cache (no heap use).
 int side_tensor_map_uncached(const void* side, int pages, int hkv, int hd, int box_rows, CUtensorMap* out);
 
+// 2-D TMA descriptor of an fp8 side cache uint8 [pages][hkv][2][2][128][128] seen as rows of
+// 128 bytes, box 128 x 128, 128-byte swizzle (cached like side_tensor_map).
+int fp8_side_tensor_map(const void* side8, int pages, int hkv, CUtensorMap* out);
+
 int device_sm_count();
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current device. The attribute

@@ -28,21 +28,25 @@
 // conversion saturates at +-65504), since an MMA takes both operands in one type. Q and K stay
 // bf16 for S^T = K . Q^T.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "far_read.cuh"
 
 namespace fold {
 
-template <int HD_, int NT_, int TK_, int HG_>
+// FP8: the side cache holds e4m3 K rows and V^T (fp8_side layout below); head size 128 only, so
+// one 128-byte row of K (or of V^T over 128 keys) is one TMA box row.
+template <int HD_, int NT_, int TK_, int HG_, bool FP8_ = false>
 struct FarCfg {
   static constexpr int HD = HD_, NT = NT_, TK = TK_, HG = HG_;
+  static constexpr bool FP8 = FP8_;
   static constexpr int ROWS = 8 * NT;
   static constexpr int NW = 8;  // warps; thread 0 also issues the TMA copies
   static constexpr int NTHREADS = NW * 32;
   static constexpr int KBOX = HD / 64;  // 64-column boxes per K (and per V) row block
   static constexpr int BOX_BYTES = TK * 128;
-  static constexpr int STAGE_BYTES = 2 * KBOX * BOX_BYTES;
+  static constexpr int STAGE_BYTES = FP8 ? 2 * BOX_BYTES : 2 * KBOX * BOX_BYTES;
   static constexpr int MT = TK / 16;  // key m-tiles per tile (one per QK warp column)
   static constexpr int NG = NW / MT;  // QK warps sharing one m-tile split the n-tiles
   static constexpr int QNT = (NT + NG - 1) / NG;
@@ -58,7 +62,8 @@ struct FarCfg {
   static constexpr int ROW_BYTES = 2 * 64 * 4;
   static constexpr int FIXED = Q_BYTES + P_BYTES + RED_BYTES + ROW_BYTES + 8 * 8 + 1024;
   static constexpr int NSTAGE_FIT = (kSmemLimit - FIXED) / STAGE_BYTES;
-  static constexpr int NSTAGE = NSTAGE_FIT > 4 ? 4 : NSTAGE_FIT;
+  static constexpr int NSTAGE_MAX = FP8 ? 6 : 4;  // at most 8: the barriers share 64 bytes
+  static constexpr int NSTAGE = NSTAGE_FIT > NSTAGE_MAX ? NSTAGE_MAX : NSTAGE_FIT;
   static constexpr int OFF_Q = NSTAGE * STAGE_BYTES;
   static constexpr int OFF_P = OFF_Q + Q_BYTES;
   static constexpr int OFF_RED = OFF_P + P_BYTES;
@@ -71,7 +76,26 @@ struct FarCfg {
   static_assert(PV_MT >= 1 && PV_KS >= 1, "warp split");
   static_assert(ROWS * HD * 4 <= NSTAGE * STAGE_BYTES, "epilogue staging");
   static_assert(TK <= 256 && 256 % TK == 0, "tiles stay inside one 256-entry page");
+  static_assert(!FP8 || (HD == 128 && TK == 128), "fp8 side cache: head size 128, tiles of 128 keys");
 };
+
+// The fp8 side cache: uint8 [pages][hkv][2 planes][2 halves][128 rows][128 bytes]. Plane 0 holds
+// K: row r of half kh is key kh * 128 + r of the page, its 128 bytes the e4m3 head dims. Plane 1
+// holds V^T: row d of half kh is head dim d, byte c the e4m3 value of key kh * 128 + c. So a tile
+// of 128 keys is one 16 KB box of K and one of V^T, and a V^T row gives the keys of one head dim
+// in consecutive bytes (the order an MMA fragment of V^T takes them in). Row of a (page, head,
+// plane, half) block in the 2-D view [rows][128 bytes]:
+__device__ __forceinline__ int fp8_side_row(int page, int hkv, int h, int plane, int half) {
+  return (((page * hkv + h) * 2 + plane) * 2 + half) * 128;
+}
+
+// FP8 fragment order: an ldmatrix of byte pairs gives a thread the bytes [4 t4, 4 t4 + 4) of a
+// 16-byte chunk, while an f16 MMA fragment takes k = (2 t4, 2 t4 + 1) and (2 t4 + 8, 2 t4 + 9).
+// So within each group of 16, element p of the chunk (a head dim of K, a key of V^T) is used as k
+// slot fp8_slot(p): Q is stored with its head dims at these slots, and P^T with its keys.
+__host__ __device__ constexpr int fp8_slot(int p) {
+  return (p >> 1) + 7 * ((p >> 1) & 1) + (p & 1);
+}
 
 
 // Issues the TMA copies of tile `tile` (index in this cache) of head h into stage `st`.
@@ -81,10 +105,16 @@ __device__ __forceinline__ void issue_tile(unsigned char* smem, uint64_t* full, 
   mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
   const int64_t lp = static_cast<int64_t>(tile) * C::TK;
   const int page = static_cast<int>(lp >> 8), off = static_cast<int>(lp & 255);
-  const int c2 = page * hkv + h;
   unsigned char* dst = smem + st * C::STAGE_BYTES;
+  if constexpr (C::FP8) {  // the K box, then the V^T box, of the tile's half of its page
+    const int half = off >> 7;
+    tma_load_2d(dst, map, &full[st], 0, fp8_side_row(page, hkv, h, 0, half), pol);
+    tma_load_2d(dst + C::BOX_BYTES, map, &full[st], 0, fp8_side_row(page, hkv, h, 1, half), pol);
+  } else {
+    const int c2 = page * hkv + h;
 #pragma unroll
-  for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
+    for (int b = 0; b < 2 * C::KBOX; ++b) tma_load_3d(dst + b * C::BOX_BYTES, map, &full[st], b * 64, off, c2, pol);
+  }
 }
 
 // Window read: the cache block that holds a warp's rows of the tile at tpos (the warp's TK / 8
@@ -220,11 +250,30 @@ __device__ __forceinline__ void rotate_query_vec(const FarParams& p, const Query
         const float2 x = __bfloat1622float2(xa[j]), xp = __bfloat1622float2(xb[j]);
         const float c_0 = cs[2 * j], c_1 = cs[2 * j + 1];
         const float s_0 = sgn * sn[2 * j], s_1 = sgn * sn[2 * j + 1];
-        oa[j] = pack_bf16(x.x * c_0 - xp.x * s_0, x.y * c_1 - xp.y * s_1);
-        ob[j] = pack_bf16(xp.x * c_0 + x.x * s_0, xp.y * c_1 + x.y * s_1);
+        const float a0 = x.x * c_0 - xp.x * s_0, a1 = x.y * c_1 - xp.y * s_1;
+        const float b0 = xp.x * c_0 + x.x * s_0, b1 = xp.y * c_1 + x.y * s_1;
+        oa[j] = C::FP8 ? pack_f16_sat(a0, a1) : pack_bf16(a0, a1);
+        ob[j] = C::FP8 ? pack_f16_sat(b0, b1) : pack_bf16(b0, b1);
       }
     } else {
       off_a = 2 * RH * (rh8 > 0) + 16 * (c - rh8), off_b = off_a + 8;
+      if constexpr (C::FP8) {
+        uint32_t* oa = reinterpret_cast<uint32_t*>(&ya);
+        uint32_t* ob = reinterpret_cast<uint32_t*>(&yb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) oa[j] = bf16x2_to_f16x2(oa[j]), ob[j] = bf16x2_to_f16x2(ob[j]);
+      }
+    }
+    if constexpr (C::FP8) {  // f16, each pair of head dims at its fp8 fragment slot
+      const uint32_t* wa = reinterpret_cast<const uint32_t*>(&ya);
+      const uint32_t* wb = reinterpret_cast<const uint32_t*>(&yb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int da = off_a + 2 * j, db = off_b + 2 * j;
+        *reinterpret_cast<uint32_t*>(Qs + rho * C::QSTRIDE + (da & ~15) + fp8_slot(da & 15)) = wa[j];
+        *reinterpret_cast<uint32_t*>(Qs + rho * C::QSTRIDE + (db & ~15) + fp8_slot(db & 15)) = wb[j];
+      }
+      continue;  // no far-query output for the fp8 read
     }
     *reinterpret_cast<uint4*>(Qs + rho * C::QSTRIDE + off_a) = ya;
     *reinterpret_cast<uint4*>(Qs + rho * C::QSTRIDE + off_b) = yb;
@@ -295,6 +344,7 @@ template <class C, bool WIN>
 __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtensorMap* vmap, const FarParams& p,
                                            int split, int h, int nsplits, int range_begin = -1,
                                            int range_tiles = 0) {
+  static_assert(!(WIN && C::FP8), "the window read takes the drafter's bf16 cache");
   constexpr int HD = C::HD, NT = C::NT, TK = C::TK, ROWS = C::ROWS, NTH = C::NTHREADS;
   constexpr int NSTAGE = C::NSTAGE, QNT = C::QNT, PV_MT = C::PV_MT, MT = C::MT, NG = C::NG;
   extern __shared__ unsigned char smem_raw[];
@@ -396,11 +446,16 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
           } else {
             y = x;
           }
-          const __nv_bfloat16 yb = __float2bfloat16_rn(y);
-          if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
-          Qs[rho * C::QSTRIDE + d] = yb;
+          if constexpr (C::FP8) {
+            const __half yh = __float2half_rn(y);
+            *reinterpret_cast<__half*>(Qs + rho * C::QSTRIDE + (d & ~15) + fp8_slot(d & 15)) = yh;
+          } else {
+            const __nv_bfloat16 yb = __float2bfloat16_rn(y);
+            if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
+            Qs[rho * C::QSTRIDE + d] = yb;
+          }
         } else {
-          Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);
+          Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);  // zero bits: 0 in f16 as well
         }
       }
     }
@@ -484,6 +539,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   bool timed_out = false;
   int consumed = 0;
   const uint32_t p_base = smem_u32(smem + C::OFF_P);
+  // fp8: the K scale of this head multiplies every logit, the V scale the output
+  float scale_log2 = p.scale_log2, out_scale = 1.f;
+  if constexpr (C::FP8) scale_log2 *= __ldg(p.k_scale + h), out_scale = __ldg(p.v_scale + h);
 
   for (int it = 0; it < ntiles; ++it) {
     const int st = it % NSTAGE;
@@ -503,11 +561,19 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       // ---- S^T = K . Q^T for keys [mt*16, mt*16+16) of the tile
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
-        const int row = mt * 16 + (lane & 15);
-        const int chunk = (kk & 3) * 2 + (lane >> 4);
-        const uint32_t a = kv_base + (kk >> 2) * C::BOX_BYTES + row * 128 + ((chunk ^ (row & 7)) << 4);
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(a, a0, a1, a2, a3);
+        if constexpr (C::FP8) {
+          // e4m3 K: byte pairs of keys g4 and g4 + 8, head dims [16 kk + 4 t4, +4) -> f16 pairs
+          const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          uint32_t r0, r1;
+          ldsm_x2(kv_base + row * 128 + ((kk ^ (row & 7)) << 4), r0, r1);
+          e4m3x4_to_f16(r0, a0, a2);
+          e4m3x4_to_f16(r1, a1, a3);
+        } else {
+          const int row = mt * 16 + (lane & 15);
+          const int chunk = (kk & 3) * 2 + (lane >> 4);
+          ldsm_x4(kv_base + (kk >> 2) * C::BOX_BYTES + row * 128 + ((chunk ^ (row & 7)) << 4), a0, a1, a2, a3);
+        }
 #pragma unroll
         for (int j = 0; j < QNT; ++j) {
           if (nt_lo + j < NT) {
@@ -520,7 +586,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
                   qs_base + (((nt_lo + j) * 8 + (lane & 7)) * C::QSTRIDE + kk * 16 + ((lane >> 3) & 1) * 8) * 2;
               ldsm_x2(qa, b0, b1);
             }
-            mma_bf16(x[j], a0, a1, a2, a3, b0, b1);
+            if constexpr (C::FP8)
+              mma_f16(x[j], a0, a1, a2, a3, b0, b1);
+            else
+              mma_bf16(x[j], a0, a1, a2, a3, b0, b1);
           }
         }
       }
@@ -530,7 +599,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         for (int j = 0; j < QNT; ++j) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float v = fmaf(x[j][e], p.scale_log2, lim[j][e & 1] > 0 ? 0.f : -INFINITY);
+            const float v = fmaf(x[j][e], scale_log2, lim[j][e & 1] > 0 ? 0.f : -INFINITY);
             x[j][e] = v;
             exceed |= v > MQ(j, e & 1) + kRaise;
           }
@@ -544,7 +613,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
             const int64_t key = key0 + (e >> 1) * 8;
             bool vis = key < lim[j][c];
             if constexpr (WIN) vis = vis && key >= llo[j][c];
-            const float v = vis ? x[j][e] * p.scale_log2 : -INFINITY;
+            const float v = vis ? x[j][e] * scale_log2 : -INFINITY;
             x[j][e] = v;
             exceed |= v > MQ(j, c) + kRaise;
           }
@@ -564,9 +633,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
           ls[j][1] = p1 + p3;
           if (nt_lo + j < NT) {
             const int r0 = (nt_lo + j) * 8 + t4 * 2;
-            const int k0 = mt * 16 + g4;
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pa));
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pb));
+            // P^T row of keys g4 and g4 + 8 (fp8: their fragment slots, the order V^T gives keys in)
+            const int ka = mt * 16 + (C::FP8 ? fp8_slot(g4) : g4), kb = mt * 16 + (C::FP8 ? fp8_slot(g4 + 8) : g4 + 8);
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (ka * C::PSTRIDE + r0) * 2), "r"(pa));
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (kb * C::PSTRIDE + r0) * 2), "r"(pb));
           }
         }
       }
@@ -642,9 +712,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         ls[j][1] = p1 + p3;
         if (nt_lo + j < NT) {
           const int r0 = (nt_lo + j) * 8 + t4 * 2;
-          const int k0 = mt * 16 + g4;
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (k0 * C::PSTRIDE + r0) * 2), "r"(pa));
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + ((k0 + 8) * C::PSTRIDE + r0) * 2), "r"(pb));
+          // P^T row of keys g4 and g4 + 8 (fp8: their fragment slots, the order V^T gives keys in)
+          const int ka = mt * 16 + (C::FP8 ? fp8_slot(g4) : g4), kb = mt * 16 + (C::FP8 ? fp8_slot(g4 + 8) : g4 + 8);
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (ka * C::PSTRIDE + r0) * 2), "r"(pa));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (kb * C::PSTRIDE + r0) * 2), "r"(pb));
         }
       }
       named_bar_sync(2, NTH);
@@ -670,14 +741,22 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
 #pragma unroll
       for (int a = 0; a < PV_MT; ++a) {
         const int ht = hg * PV_MT + a;
-        const int q = lane >> 3;
-        const int key_row = kk * 16 + (q >> 1) * 8 + (lane & 7);
-        const int chunk = (ht & 3) * 2 + (q & 1);
-        const uint32_t va =
-            kv_base + (C::KBOX + (ht >> 2)) * C::BOX_BYTES + key_row * 128 + ((chunk ^ (key_row & 7)) << 4);
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(va, a0, a1, a2, a3);
-        a0 = bf16x2_to_f16x2(a0), a1 = bf16x2_to_f16x2(a1), a2 = bf16x2_to_f16x2(a2), a3 = bf16x2_to_f16x2(a3);
+        if constexpr (C::FP8) {
+          // e4m3 V^T: byte pairs of head dims g4 and g4 + 8, keys [16 kk + 4 t4, +4) -> f16 pairs
+          const int row = ht * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          uint32_t r0, r1;
+          ldsm_x2(kv_base + C::BOX_BYTES + row * 128 + ((kk ^ (row & 7)) << 4), r0, r1);
+          e4m3x4_to_f16(r0, a0, a2);
+          e4m3x4_to_f16(r1, a1, a3);
+        } else {
+          const int q = lane >> 3;
+          const int key_row = kk * 16 + (q >> 1) * 8 + (lane & 7);
+          const int chunk = (ht & 3) * 2 + (q & 1);
+          ldsm_x4_t(kv_base + (C::KBOX + (ht >> 2)) * C::BOX_BYTES + key_row * 128 + ((chunk ^ (key_row & 7)) << 4),
+                    a0, a1, a2, a3);
+          a0 = bf16x2_to_f16x2(a0), a1 = bf16x2_to_f16x2(a1), a2 = bf16x2_to_f16x2(a2), a3 = bf16x2_to_f16x2(a3);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_f16(oacc[a][nt], a0, a1, a2, a3, bfr[nt][0], bfr[nt][1]);
       }
@@ -745,7 +824,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
 #pragma unroll
     for (int q = 0; q < MT; ++q) L += red[q * ROWS + tid];
     const float m = row_m[tid];
-    row_inv[tid] = L > 0.f ? 1.f / L : 0.f;
+    row_inv[tid] = L > 0.f ? out_scale / L : 0.f;
     if (tid < nrows) {
       const int r = tid / G, hq = h * G + (tid - r * G);
       p.lse_part[l_split + static_cast<int64_t>(hq) * p.n + r] = L > 0.f ? (m + __log2f(L)) * kLn2 : -INFINITY;

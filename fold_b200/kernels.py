@@ -330,6 +330,73 @@ def append(k, v, positions, slots, side, *, pos_lo=0, skip_foreign=False, err=No
               _stream(side))
 
 
+FP8_HEAD_DIM = 128  # the fp8 side cache's head size
+
+
+def fp8_side_shape(pages: int, hkv: int):
+    """Shape of an fp8 side cache of `pages` pages (uint8; layout in include/fold_b200.h)."""
+    return (int(pages), int(hkv), 2, 2, 128, 128)
+
+
+def _check_fp8_side(side8, k_scale, v_scale):
+    if side8.dtype != torch.uint8 or side8.dim() != 6 or tuple(side8.shape[2:]) != (2, 2, 128, 128) \
+            or not side8.is_contiguous():
+        raise FoldError("fp8 side cache: a contiguous uint8 [pages, Hkv, 2, 2, 128, 128] tensor")
+    hkv = side8.shape[1]
+    for s in (k_scale, v_scale):
+        if s.dtype != torch.float32 or s.numel() != hkv or not s.is_contiguous():
+            raise FoldError("fp8 side cache: k_scale and v_scale are contiguous float32 [Hkv]")
+
+
+def append_fp8(k, v, positions, slots, side8, k_scale, v_scale, *, pos_lo=0, skip_foreign=False, err=None):
+    """Quantising append into an fp8 side cache: K [ctx, Hkv, 128] (before RoPE) and V, bf16, are
+    divided by the per-head scales and rounded to e4m3 (fold_append_fp8)."""
+    _require_cuda(k, v, positions, slots, side8, k_scale, v_scale, err)
+    ctx = k.shape[0]
+    if ctx == 0:
+        return
+    _check_fp8_side(side8, k_scale, v_scale)
+    hkv = side8.shape[1]
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise FoldError("append_fp8: K and V must be bfloat16")
+    if k.shape[1:] != (hkv, FP8_HEAD_DIM) or v.shape[1:] != (hkv, FP8_HEAD_DIM) or v.shape[0] < ctx:
+        raise FoldError("append_fp8: K/V must be [ctx, Hkv, 128] matching the side cache")
+    if k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise FoldError("append_fp8: the head dimension of K and V must be contiguous")
+    if positions.dim() != 1 or slots.dim() != 1 or positions.shape[0] < ctx or slots.shape[0] < ctx:
+        raise FoldError("append_fp8: positions and slots need one entry per K/V row")
+    positions = positions[:ctx].to(torch.int64).contiguous()
+    slots = slots[:ctx].to(torch.int64).contiguous()
+    _lib.call("fold_append_fp8", _p(k), k.stride(0), k.stride(1), _p(v), v.stride(0), v.stride(1), _p(positions),
+              _p(slots), ctx, _p(side8), side8.shape[0], hkv, FP8_HEAD_DIM, _p(k_scale), _p(v_scale), int(pos_lo),
+              int(bool(skip_foreign)), _p(err), _stream(side8))
+
+
+def far_read_fp8(q, qsl, seq_lens, side8, k_scale, v_scale, o_part, lse_part, *, window, block, far_distance,
+                 softmax_scale, table=None, rot_dim=None, far_len=None, pos_lo=0, capacity=None, err=None):
+    """far_read of an fp8 side cache (fold_far_read_fp8): the same split partials, with K and V
+    the e4m3 values times their per-head scales."""
+    _require_cuda(q, qsl, seq_lens, side8, k_scale, v_scale, o_part, lse_part, table, far_len, err)
+    _check_lengths(qsl, seq_lens)
+    _check_fp8_side(side8, k_scale, v_scale)
+    n, hq, d = q.shape
+    if d != FP8_HEAD_DIM or q.dtype != torch.bfloat16:
+        raise FoldError("far_read_fp8: q must be bfloat16 with head size 128")
+    splits = _check_partials(o_part, lse_part, n, hq, d, "far_read_fp8")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    pages = side8.shape[0]
+    if capacity is None:
+        capacity = int(pos_lo) + (pages - 1) * SIDE_BLOCK
+    if table is not None and rot_dim is None:
+        rot_dim = table.shape[1]
+    _lib.call("fold_far_read_fp8", _p(q), q.stride(0), q.stride(1), _p(qsl), _p(seq_lens), _p(table),
+              0 if table is None else table.shape[0], 0 if table is None else int(rot_dim), _p(side8), pages,
+              int(pos_lo), int(capacity), _p(far_len), _p(k_scale), _p(v_scale), _p(o_part), _p(lse_part), splits, n,
+              hq, side8.shape[1], d, int(window), int(block), int(far_distance), float(softmax_scale), _p(err),
+              _stream(q))
+
+
 def gather(side, positions, *, pos_lo=0, err=None):
     """K, V [m, Hkv, D] of the given absolute positions of a side cache."""
     _require_cuda(side, positions, err)

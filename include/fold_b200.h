@@ -62,6 +62,19 @@ int fold_append(const void* k, int64_t k_stride_tok, int64_t k_stride_head, cons
                 int64_t v_stride_head, const int64_t* positions, const int64_t* slots, int ctx, void* side,
                 int pages, int hkv, int hd, int64_t pos_lo, int skip_foreign, int* err, void* stream);
 
+/* Side-cache append into the fp8 side cache (the storage-format option of the far memory; no
+ * reference counterpart: the reference stores the side cache in the KV-cache dtype,
+ * fold/attention.py:66). K/V rows as fold_append (bf16, before RoPE), quantised to e4m3 (round to
+ * nearest even, saturating at +-448) after division by the per-KV-head scales k_scale, v_scale
+ * (float [hkv], device). side8: uint8 [pages][hkv][2][2][128][128]: per (page, head), plane 0
+ * holds the K rows of keys [0, 128) and [128, 256) of the page (128 bytes each), plane 1 their V
+ * transposed (row = head dim, byte = key). Head size 128 only. Rows with slot < 0 go to the
+ * dummy slot (the last position of the last page), as fold_append. */
+int fold_append_fp8(const void* k, int64_t k_stride_tok, int64_t k_stride_head, const void* v,
+                    int64_t v_stride_tok, int64_t v_stride_head, const int64_t* positions, const int64_t* slots,
+                    int ctx, void* side8, int pages, int hkv, int hd, const float* k_scale, const float* v_scale,
+                    int64_t pos_lo, int skip_foreign, int* err, void* stream);
+
 /* Read back K and V of absolute positions into k_out, v_out [m, hkv, hd] bf16 (contiguous).
  * The inverse of fold_append for checks and shard moves; no reference counterpart beyond the
  * FlashAttention page read of fold/attention.py:165. */
@@ -129,6 +142,18 @@ int fold_window_read(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                      const int* block_table, int block_table_len, int window_left, int window_right, int causal,
                      float softmax_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
                      int* err, void* stream);
+
+/* Far-memory read of an fp8 side cache (fold_append_fp8): the work of fold_far_read with the keys
+ * and values dequantised by k_scale, v_scale (float [hkv], device): K and V of the side cache are
+ * e4m3 (exact in f16), the tiles f16 MMAs with f32 accumulation, the query rotated in float32 and
+ * rounded to f16. Half the bytes of the bf16 side cache per key. Head size 128, at most 64 query
+ * rows per KV head; no qf output. No reference counterpart (a storage-format option of the far
+ * memory, beside fold_far_read). */
+int fold_far_read_fp8(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,
+                      const int* seq_lens, const float* rope_table, int table_rows, int rot_dim, const void* side8,
+                      int pages, int64_t pos_lo, int64_t capacity, int* far_len, const float* k_scale,
+                      const float* v_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
+                      int window, int block, int far_distance, float softmax_scale, int* err, void* stream);
 
 /* The far read and the window read of one draft step in one launch. Replaces, for a full-attention
  * FOLD layer, far_query + both FlashAttention reads of fold/attention.py:162-170. Arguments as
