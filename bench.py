@@ -970,18 +970,15 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
             step(i, last)
         compute.wait_stream(down)
 
-    done = torch.cuda.Event()
-
     def run_serial(first, last):
         """One step after the other as a drafter must take them (step i + 1's query depends on
-        step i's output): upload, replay, read back, wait for the output on the host."""
+        step i's output): upload, replay, read back, each ordered after the last on one stream,
+        so no copy overlaps any step's compute."""
         sl = slots[0]
         for i in range(first, last):
             sl.d_in.copy_(h_in[i], non_blocking=True)
             sl.graph.replay()
             h_out[0].copy_(sl.out, non_blocking=True)
-            done.record(compute)
-            done.synchronize()
 
     def timed(fn):
         """fn(warmup + ...) steps timed with events on the compute stream after untimed passes
@@ -1027,8 +1024,8 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
         "CUDA graph and replayed per step")
     return {"value": round(us_serial, 3), "unit": "us/draft-step",
             "h2d_bytes_per_step": rec, "d2h_bytes_per_step": B * hq * hd * 2,
-            "api": api + "; per step, serially: one pinned host->device copy of the step's inputs, the replay, one "
-                         "device->host copy of its output, and a host wait for that output before the next step",
+            "api": api + "; per step, serially on one stream: one pinned host->device copy of the step's inputs, "
+                         "the replay, one device->host copy of its output, then the next step's copy",
             "pipelined": {"value": round(us_pipelined, 3), "unit": "us/draft-step",
                           "how": "the same steps with the copies on their own streams, double-buffered so that "
                                  "step i + 1's upload and step i - 1's read-back overlap step i (throughput of "
