@@ -24,6 +24,7 @@ struct AppendParams {
 };
 
 __global__ void append_kernel(const AppendParams p) {
+  release_dependents();  // the far read behind it may be scheduled; it waits for this grid to complete
   const int kc = p.hd >> 3;  // 16-byte chunks per K (and per V) row
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < p.total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -79,6 +80,7 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float
 // Index layout: idx = ((chunk * hkv + h) * 2 + plane) * ctx + token, so consecutive threads walk
 // consecutive tokens of one (chunk, head, plane).
 __global__ void append_fp8_kernel(const AppendFp8Params p) {
+  release_dependents();
   const int64_t total = p.ctx * p.hkv * 2 * 8;  // 8 chunks of 16 head dims (hd 128)
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {

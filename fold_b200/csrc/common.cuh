@@ -50,6 +50,14 @@ __device__ __forceinline__ void mbar_inval(uint64_t* bar) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Programmatic dependent launch. wait_for_producer returns once the grid this one was launched
+// behind (with programmatic stream serialisation) has completed and its writes are visible; it
+// returns at once for a grid launched the ordinary way. Kernels launched with that attribute
+// call it before their first access to global memory, so they only start early, never read or
+// write early. release_dependents lets the next such launch on the stream be scheduled once
+// every block of this grid has executed it (or exited).
+__device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void release_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

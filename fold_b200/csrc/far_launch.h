@@ -27,18 +27,18 @@ int make_window_params(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        float softmax_scale, float* o_part, float* lse_part, int splits, int n, int hq, int hkv, int hd,
                        int* err, FarParams* out);
 
-// Calls f.run<FarCfg<HD, nt, TK, HG, FP8>>() for nt in 1..8 (n * G query rows in n8 tiles).
-template <int HD, int TK, int HG, class F, bool FP8 = false>
+// Calls f.run<FarCfg<HD, nt, TK, HG, FP8, NW>>() for nt in 1..8 (n * G query rows in n8 tiles).
+template <int HD, int TK, int HG, class F, bool FP8 = false, int NW = 8>
 int with_row_tiles(int nt, const F& f) {
   switch (nt) {
-    case 1: return f.template run<FarCfg<HD, 1, TK, HG, FP8>>();
-    case 2: return f.template run<FarCfg<HD, 2, TK, HG, FP8>>();
-    case 3: return f.template run<FarCfg<HD, 3, TK, HG, FP8>>();
-    case 4: return f.template run<FarCfg<HD, 4, TK, HG, FP8>>();
-    case 5: return f.template run<FarCfg<HD, 5, TK, HG, FP8>>();
-    case 6: return f.template run<FarCfg<HD, 6, TK, HG, FP8>>();
-    case 7: return f.template run<FarCfg<HD, 7, TK, HG, FP8>>();
-    case 8: return f.template run<FarCfg<HD, 8, TK, HG, FP8>>();
+    case 1: return f.template run<FarCfg<HD, 1, TK, HG, FP8, NW>>();
+    case 2: return f.template run<FarCfg<HD, 2, TK, HG, FP8, NW>>();
+    case 3: return f.template run<FarCfg<HD, 3, TK, HG, FP8, NW>>();
+    case 4: return f.template run<FarCfg<HD, 4, TK, HG, FP8, NW>>();
+    case 5: return f.template run<FarCfg<HD, 5, TK, HG, FP8, NW>>();
+    case 6: return f.template run<FarCfg<HD, 6, TK, HG, FP8, NW>>();
+    case 7: return f.template run<FarCfg<HD, 7, TK, HG, FP8, NW>>();
+    case 8: return f.template run<FarCfg<HD, 8, TK, HG, FP8, NW>>();
     default: return fail(FOLD_ERR_UNSUPPORTED, "n * (hq / hkv) must be at most 64");
   }
 }

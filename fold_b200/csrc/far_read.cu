@@ -14,11 +14,13 @@ namespace fold {
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
+  wait_for_producer();
   split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarParams p) {
+  wait_for_producer();
   split_read<C, true>(nullptr, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
@@ -67,6 +69,7 @@ template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     step_read_kernel(const __grid_constant__ CUtensorMap far_map, const FarParams far, const FarParams win,
                      int* plan) {
+  wait_for_producer();
   const int S = static_cast<int>(gridDim.x), x = static_cast<int>(blockIdx.x), h = static_cast<int>(blockIdx.y);
   const StepSplit sp = step_split<C>(far, win, S);
   if (x == 0 && h == 0 && threadIdx.x == 0) *plan = sp.w;
@@ -219,8 +222,8 @@ struct FarLaunch {
     if (s) return s;
     static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(far_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(far_read)")) return e;
-    far_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
-    return check_launch("far_read_kernel");
+    return launch_behind(far_read_kernel<C>, dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream,
+                         "far_read_kernel", map, prm);
   }
 };
 
@@ -231,8 +234,8 @@ struct WindowLaunch {
   int run() const {
     static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(window_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(window_read)")) return e;
-    window_read_kernel<C><<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(prm);
-    return check_launch("window_read_kernel");
+    return launch_behind(window_read_kernel<C>, dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream,
+                         "window_read_kernel", prm);
   }
 };
 
@@ -249,8 +252,8 @@ struct StepLaunch {
     if (int s = side_tensor_map(side, pages, far.hkv, C::HD, C::TK, &map)) return s;
     static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
     if (int e = allow_smem(step_read_kernel<C>, C::SMEM, configured, "cudaFuncSetAttribute(step_read)")) return e;
-    step_read_kernel<C><<<dim3(far.splits, far.hkv), C::NTHREADS, C::SMEM, stream>>>(map, far, win, plan);
-    return check_launch("step_read_kernel");
+    return launch_behind(step_read_kernel<C>, dim3(far.splits, far.hkv), C::NTHREADS, C::SMEM, stream,
+                         "step_read_kernel", map, far, win, plan);
   }
 };
 

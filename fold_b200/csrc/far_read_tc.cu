@@ -351,6 +351,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, h = blockIdx.y;
   const int G = p.group, nrows = p.n * G;
+  wait_for_producer();
 
   // Step geometry, from the device-side lengths (fold/kernels.py:24-30).
   const int qlen = p.qsl[1] - p.qsl[0];
@@ -626,6 +627,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     }
 
     // -------------------------------------------------------------- epilogue
+    release_dependents();  // the merge may be scheduled; it waits for this grid to complete
     // row sums over the 128 keys of each tile position
 #pragma unroll
     for (int c = 0; c < HALF; ++c) {
@@ -695,8 +697,8 @@ int launch_tc(const FarParams& prm, const void* side, int pages, bool cached, cu
   auto kern = far_read_tc_kernel<C>;
   static std::atomic<uint64_t> configured{0};  // per instantiation, one bit per device
   if (int e = allow_smem(kern, C::SMEM, configured, "cudaFuncSetAttribute(far_read_tc)")) return e;
-  kern<<<dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream>>>(map, prm);
-  return check_launch("far_read_tc_kernel");
+  return launch_behind(kern, dim3(prm.splits, prm.hkv), C::NTHREADS, C::SMEM, stream, "far_read_tc_kernel", map,
+                       prm);
 }
 
 template <int HD>

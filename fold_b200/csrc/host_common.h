@@ -52,6 +52,22 @@ int allow_smem(K kern, int bytes, std::atomic<uint64_t>& configured, const char*
   return FOLD_OK;
 }
 
+// Launches `kern` with programmatic stream serialisation: its blocks may be scheduled while the
+// previous kernel on the stream is still running, once every block of that kernel has executed
+// release_dependents (or exited). Only kernels that call wait_for_producer before their first
+// global-memory access are launched this way.
+template <class... KArgs, class... Args>
+int launch_behind(void (*kern)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t stream, const char* what,
+                  Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid, cfg.blockDim = dim3(threads), cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream, cfg.attrs = attr, cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...), what);
+}
+
 // Far read into caller-given partial buffers with the descriptor built on the stack; the
 // arguments and checks are those of fold_far_read.
 int far_read_uncached(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const int* qsl,

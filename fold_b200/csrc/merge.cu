@@ -15,6 +15,7 @@ namespace fold {
 template <bool FINAL>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeParams p, int slices, int hd) {
   __shared__ SliceSums sums;
+  wait_for_producer();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slice = blockIdx.x % slices, th = blockIdx.x / slices;
   const int t = th / p.hq, h = th - (th / p.hq) * p.hq;
@@ -43,6 +44,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
 __global__ void __launch_bounds__(kMergeWarps * 32)
     merge_partials_kernel(const MergeParams pw, const MergeParams pf, const int* plan, int slices, int hd) {
   __shared__ SliceSums sums;
+  wait_for_producer();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slice = blockIdx.x % slices, th = blockIdx.x / slices;
   const int t = th / pf.hq, h = th - (th / pf.hq) * pf.hq;
@@ -67,11 +69,10 @@ static int merge_launch(const MergeParams& p, int hd, bool combine, cudaStream_t
   const int slices = hd > kSlice ? hd / kSlice : 1;
   const int64_t blocks = static_cast<int64_t>(p.n) * p.hq * slices;
   if (blocks > 2147483647) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge: too many rows");
+  const dim3 grid(static_cast<unsigned>(blocks));
   if (combine)
-    merge_kernel<false><<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, stream>>>(p, slices, hd);
-  else
-    merge_kernel<true><<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, stream>>>(p, slices, hd);
-  return check_launch(combine ? "combine_kernel" : "merge_kernel");
+    return launch_behind(merge_kernel<false>, grid, kMergeWarps * 32, 0, stream, "combine_kernel", p, slices, hd);
+  return launch_behind(merge_kernel<true>, grid, kMergeWarps * 32, 0, stream, "merge_kernel", p, slices, hd);
 }
 
 int merge_contiguous_partials(const void* o_l, int64_t ol_stride_tok, int64_t ol_stride_head, const float* lse_l,
@@ -158,9 +159,8 @@ int fold_merge_partials(const float* o_wpart, const float* lse_wpart, int wsplit
   const int slices = hd > kSlice ? hd / kSlice : 1;
   const int64_t blocks = static_cast<int64_t>(n) * hq * slices;
   if (blocks > 2147483647) return fail(FOLD_ERR_INVALID_ARGUMENT, "merge partials: too many rows");
-  merge_partials_kernel<<<static_cast<unsigned>(blocks), kMergeWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      pw, pf, plan, slices, hd);
-  return check_launch("merge_partials_kernel");
+  return launch_behind(merge_partials_kernel, dim3(static_cast<unsigned>(blocks)), kMergeWarps * 32, 0,
+                       static_cast<cudaStream_t>(stream), "merge_partials_kernel", pw, pf, plan, slices, hd);
 }
 
 int fold_combine(const float* o_part, const float* lse_part, int splits, float* o_out, float* lse_out, int n, int hq,

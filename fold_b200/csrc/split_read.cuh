@@ -37,12 +37,12 @@ namespace fold {
 
 // FP8: the side cache holds e4m3 K rows and V^T (fp8_side layout below); head size 128 only, so
 // one 128-byte row of K (or of V^T over 128 keys) is one TMA box row.
-template <int HD_, int NT_, int TK_, int HG_, bool FP8_ = false>
+template <int HD_, int NT_, int TK_, int HG_, bool FP8_ = false, int NW_ = 8>
 struct FarCfg {
   static constexpr int HD = HD_, NT = NT_, TK = TK_, HG = HG_;
   static constexpr bool FP8 = FP8_;
   static constexpr int ROWS = 8 * NT;
-  static constexpr int NW = 8;  // warps; thread 0 also issues the TMA copies
+  static constexpr int NW = NW_;  // warps; thread 0 also issues the TMA copies
   static constexpr int NTHREADS = NW * 32;
   static constexpr int KBOX = HD / 64;  // 64-column boxes per K (and per V) row block
   static constexpr int BOX_BYTES = TK * 128;
@@ -765,6 +765,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   }
 
   // -------------------------------------------------------------- epilogue
+  release_dependents();  // the merge may be scheduled; it waits for this grid to complete
   const int64_t o_split = static_cast<int64_t>(split) * p.n * p.hq * HD;
   const int64_t l_split = static_cast<int64_t>(split) * p.hq * p.n;
   if (timed_out) {
