@@ -535,6 +535,36 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     if constexpr (NG == 1) return mrow[j][c];
     else return mq_own[j][c];
   };
+  // Logits are kept relative to the row maximum m (0 while a row has none): x * scale_log2 - m in
+  // one FFMA, and P = 2^that. The CTA raises a maximum when some relative logit exceeds THR(j, c):
+  // kRaise, or -inf while the row has no maximum, so that its first finite logit sets one. The
+  // far read needs no per-row threshold: its first tile, which always sets the maxima, holds a
+  // visible key of every row that sees any key of the split (a row sees a prefix of the
+  // positions). Padding rows of the far read have zero queries, so logit 0 and P = 1 in open
+  // tiles: their columns of P^T and O are never written out.
+  float thr[WIN ? QNT : 1][2];
+#pragma unroll
+  for (int j = 0; j < (WIN ? QNT : 1); ++j) thr[j][0] = thr[j][1] = -INFINITY;
+  auto THR = [&](int j, int c) -> float {
+    if constexpr (WIN) return thr[j][c];
+    else return kRaise;
+  };
+  auto neg_max = [&](int j, int c) -> float { return MQ(j, c) == -INFINITY ? 0.f : -MQ(j, c); };
+  // P of QK n-tile j from its relative logits moved by sh[c], into P^T and the row sums.
+  auto store_p = [&](int j, const float (&sh)[2], float (&xs)[QNT][4], float (&lsum)[QNT][2], uint32_t pt) {
+    const float p0 = fast_exp2(xs[j][0] + sh[0]), p1 = fast_exp2(xs[j][1] + sh[1]);
+    const float p2 = fast_exp2(xs[j][2] + sh[0]), p3 = fast_exp2(xs[j][3] + sh[1]);
+    const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
+    lsum[j][0] = p0 + p2;
+    lsum[j][1] = p1 + p3;
+    if (nt_lo + j < NT) {
+      const int r0 = (nt_lo + j) * 8 + t4 * 2;
+      // P^T row of keys g4 and g4 + 8 (fp8: their fragment slots, the order V^T gives keys in)
+      const int ka = mt * 16 + (C::FP8 ? fp8_slot(g4) : g4), kb = mt * 16 + (C::FP8 ? fp8_slot(g4 + 8) : g4 + 8);
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (ka * C::PSTRIDE + r0) * 2), "r"(pa));
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (kb * C::PSTRIDE + r0) * 2), "r"(pb));
+    }
+  };
 
   bool timed_out = false;
   int consumed = 0;
@@ -593,15 +623,16 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
           }
         }
       }
-      // ---- scale, mask, exponentiate against the current row maximum
+      // ---- scale, mask, and exponentiate relative to the current row maximum
       if (!WIN && tpos + TK <= open_end) {
 #pragma unroll
         for (int j = 0; j < QNT; ++j) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float v = fmaf(x[j][e], scale_log2, lim[j][e & 1] > 0 ? 0.f : -INFINITY);
-            x[j][e] = v;
-            exceed |= v > MQ(j, e & 1) + kRaise;
+          for (int c = 0; c < 2; ++c) {
+            const float b = neg_max(j, c), t = THR(j, c);
+            x[j][c] = fmaf(x[j][c], scale_log2, b);
+            x[j][c + 2] = fmaf(x[j][c + 2], scale_log2, b);
+            exceed |= fmaxf(x[j][c], x[j][c + 2]) > t;
           }
         }
       } else {
@@ -613,32 +644,18 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
             const int64_t key = key0 + (e >> 1) * 8;
             bool vis = key < lim[j][c];
             if constexpr (WIN) vis = vis && key >= llo[j][c];
-            const float v = vis ? x[j][e] * scale_log2 : -INFINITY;
+            const float v = vis ? fmaf(x[j][e], scale_log2, neg_max(j, c)) : -INFINITY;
             x[j][e] = v;
-            exceed |= v > MQ(j, c) + kRaise;
+            exceed |= v > THR(j, c);
           }
         }
       }
       if (it == 0) {
         exceed = true;  // the first tile always sets the row maxima: skip the provisional P
       } else {
+        const float zero[2] = {0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < QNT; ++j) {
-          const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
-          const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-          const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
-          const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
-          const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
-          ls[j][0] = p0 + p2;
-          ls[j][1] = p1 + p3;
-          if (nt_lo + j < NT) {
-            const int r0 = (nt_lo + j) * 8 + t4 * 2;
-            // P^T row of keys g4 and g4 + 8 (fp8: their fragment slots, the order V^T gives keys in)
-            const int ka = mt * 16 + (C::FP8 ? fp8_slot(g4) : g4), kb = mt * 16 + (C::FP8 ? fp8_slot(g4 + 8) : g4 + 8);
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (ka * C::PSTRIDE + r0) * 2), "r"(pa));
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (kb * C::PSTRIDE + r0) * 2), "r"(pb));
-          }
-        }
+        for (int j = 0; j < QNT; ++j) store_p(j, zero, x, ls, pt);
       }
     }
 
@@ -653,7 +670,8 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         if (lane == 0) set_error(p.err, FOLD_DEVERR_TIMEOUT);
         break;
       }
-      // ---- raise the row maximum where a logit passed it by more than 2^kRaise
+      // ---- raise the row maximum where a logit passed it by more than 2^kRaise (the shared
+      // row maxima are of the logits relative to the old maximum, the same in every warp)
 #pragma unroll
       for (int j = 0; j < QNT; ++j) {
 #pragma unroll
@@ -668,6 +686,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       named_bar_sync(2, NTH);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
+        float sh[2];  // old maximum - new maximum (0 while a row has none)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int row = nt * 8 + t4 * 2 + c;
@@ -675,9 +694,12 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
 #pragma unroll
           for (int q = 1; q < MT; ++q) tm = fmaxf(tm, red[q * ROWS + row]);
           const float mo = mrow[nt][c];
+          const float meo = mo == -INFINITY ? 0.f : mo;
+          tm += meo;
           const float mn = tm > mo + kRaise ? tm : mo;
           const float f = mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
           mrow[nt][c] = mn;
+          sh[c] = meo - (mn == -INFINITY ? 0.f : mn);
 #pragma unroll
           for (int a = 0; a < PV_MT; ++a) {
             oacc[a][nt][c] *= f;
@@ -685,12 +707,15 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
           }
           if constexpr (NG == 1) {
             lq[nt][c] *= f;
+            if constexpr (WIN) thr[nt][c] = mn == -INFINITY ? -INFINITY : kRaise;
           }
         }
+        if constexpr (NG == 1) store_p(nt, sh, x, ls, pt);
       }
+      if constexpr (NG > 1) {
 #pragma unroll
-      for (int j = 0; j < QNT; ++j) {
-        if constexpr (NG > 1) {
+        for (int j = 0; j < QNT; ++j) {
+          float sh[2];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int row = min(nt_lo + j, NT - 1) * 8 + t4 * 2 + c;
@@ -698,24 +723,15 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
 #pragma unroll
             for (int q = 1; q < MT; ++q) tm = fmaxf(tm, red[q * ROWS + row]);
             const float mo = mq_own[j][c];
+            const float meo = mo == -INFINITY ? 0.f : mo;
+            tm += meo;
             const float mn = tm > mo + kRaise ? tm : mo;
             lq[j][c] *= mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
             mq_own[j][c] = mn;
+            sh[c] = meo - (mn == -INFINITY ? 0.f : mn);
+            if constexpr (WIN) thr[j][c] = mn == -INFINITY ? -INFINITY : kRaise;
           }
-        }
-        const float m0 = MQ(j, 0) == -INFINITY ? 0.f : MQ(j, 0);
-        const float m1 = MQ(j, 1) == -INFINITY ? 0.f : MQ(j, 1);
-        const float p0 = fast_exp2(x[j][0] - m0), p1 = fast_exp2(x[j][1] - m1);
-        const float p2 = fast_exp2(x[j][2] - m0), p3 = fast_exp2(x[j][3] - m1);
-        const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
-        ls[j][0] = p0 + p2;
-        ls[j][1] = p1 + p3;
-        if (nt_lo + j < NT) {
-          const int r0 = (nt_lo + j) * 8 + t4 * 2;
-          // P^T row of keys g4 and g4 + 8 (fp8: their fragment slots, the order V^T gives keys in)
-          const int ka = mt * 16 + (C::FP8 ? fp8_slot(g4) : g4), kb = mt * 16 + (C::FP8 ? fp8_slot(g4 + 8) : g4 + 8);
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (ka * C::PSTRIDE + r0) * 2), "r"(pa));
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (kb * C::PSTRIDE + r0) * 2), "r"(pb));
+          store_p(j, sh, x, ls, pt);
         }
       }
       named_bar_sync(2, NTH);
