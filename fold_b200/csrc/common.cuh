@@ -53,9 +53,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // Programmatic dependent launch. wait_for_producer returns once the grid this one was launched
 // behind (with programmatic stream serialisation) has completed and its writes are visible; it
 // returns at once for a grid launched the ordinary way. Kernels launched with that attribute
-// call it before their first access to global memory, so they only start early, never read or
-// write early. release_dependents lets the next such launch on the stream be scheduled once
-// every block of this grid has executed it (or exited).
+// call it before their first global write and before reading anything a kernel of this library
+// that releases its dependents early writes (the side cache, partials, lengths and error
+// outputs, a rotated query). release_dependents lets the next such launch on the stream be
+// scheduled once every block of this grid has executed it (or exited).
 __device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void release_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {

@@ -14,13 +14,11 @@ namespace fold {
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     far_read_kernel(const __grid_constant__ CUtensorMap map, const FarParams p) {
-  wait_for_producer();
   split_read<C, false>(&map, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
 template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1) window_read_kernel(const FarParams p) {
-  wait_for_producer();
   split_read<C, true>(nullptr, nullptr, p, blockIdx.x, blockIdx.y, p.splits);
 }
 
@@ -69,9 +67,9 @@ template <class C>
 __global__ void __launch_bounds__(C::NTHREADS, 1)
     step_read_kernel(const __grid_constant__ CUtensorMap far_map, const FarParams far, const FarParams win,
                      int* plan) {
-  wait_for_producer();
   const int S = static_cast<int>(gridDim.x), x = static_cast<int>(blockIdx.x), h = static_cast<int>(blockIdx.y);
-  const StepSplit sp = step_split<C>(far, win, S);
+  const StepSplit sp = step_split<C>(far, win, S);  // lengths only: before the producer wait
+  wait_for_producer();
   if (x == 0 && h == 0 && threadIdx.x == 0) *plan = sp.w;
   int b0, b1;  // this block's far tiles
   if (x < sp.w) {

@@ -627,7 +627,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1)
     }
 
     // -------------------------------------------------------------- epilogue
-    release_dependents();  // the merge may be scheduled; it waits for this grid to complete
+    if (!p.qf) release_dependents();  // as in split_read: the merge may be scheduled
     // row sums over the 128 keys of each tile position
 #pragma unroll
     for (int c = 0; c < HALF; ++c) {

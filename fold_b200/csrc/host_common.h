@@ -55,7 +55,7 @@ int allow_smem(K kern, int bytes, std::atomic<uint64_t>& configured, const char*
 // Launches `kern` with programmatic stream serialisation: its blocks may be scheduled while the
 // previous kernel on the stream is still running, once every block of that kernel has executed
 // release_dependents (or exited). Only kernels that call wait_for_producer before their first
-// global-memory access are launched this way.
+// global write, and before reading what such a producer writes, are launched this way.
 template <class... KArgs, class... Args>
 int launch_behind(void (*kern)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t stream, const char* what,
                   Args&&... args) {

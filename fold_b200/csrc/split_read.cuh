@@ -378,6 +378,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
                          ? max(min(range_begin + range_tiles, tiles) - t_begin, 0)
                          : static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / nsplits) - t_begin;
 
+  // Everything above read only the query, the lengths and the rope table, which no kernel that
+  // releases its dependents early writes; the side cache and every output wait for the producer.
+  wait_for_producer();
+
   uint64_t pol = 0;
   // Window read: lane 0 of each warp holds the block of the warp's rows in the next tile to be
   // issued (looked up one tile ahead, so that the lookup's latency is off the refill's path).
@@ -781,7 +785,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   }
 
   // -------------------------------------------------------------- epilogue
-  release_dependents();  // the merge may be scheduled; it waits for this grid to complete
+  // The merge may be scheduled; it waits for this grid to complete. A read that writes the rotated
+  // query (qf) releases nothing early: a far read behind it could read qf as its query before its
+  // wait.
+  if (!p.qf) release_dependents();
   const int64_t o_split = static_cast<int64_t>(split) * p.n * p.hq * HD;
   const int64_t l_split = static_cast<int64_t>(split) * p.hq * p.n;
   if (timed_out) {
