@@ -861,6 +861,7 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
 
     hq, hkv, hd, B, W = cfg["hq"], cfg["hkv"], cfg["hd"], cfg["B"], cfg["W"]
     total = args.warmup + args.steps
+    fused = args.exchange == "p2p" and args.fused  # the data plane of the device-timed step
     dummy = torch.zeros((1, hkv, 16, 2 * hd), device=dev, dtype=torch.bfloat16)
     plan = ShardPlan.for_far(length, W, B, world, rank)
     ws = FoldWorkspace(dummy, W, B, length, inv_freq=torch.ones(hd // 2, device=dev), far_distance=W + B,
@@ -919,9 +920,9 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
             ws.append(self.k, self.v, self.pos, self.slots)
             if peer is not None and sharded is None:
                 peer.read_merge(ws, self.q, qsl, self.seq, scale, o_l, lse_l, self.out)
-            elif sharded is not None and peer is not None:
+            elif sharded is not None and fused:
                 sharded.step_merge(self.q, qsl, self.seq, scale, o_l, lse_l, self.out, fused=True)
-            elif sharded is not None:
+            elif sharded is not None:  # far read, then the exchange of the step (peer or NCCL) and the merge
                 o_all, lse_all = sharded.step(self.q, qsl, self.seq, scale)
                 sharded.merge(o_l, lse_l, o_all, lse_all, self.out, qsl, self.seq)
             else:
@@ -1019,7 +1020,8 @@ def run_e2e(args, cfg, dev, side, table, H, acc, pos_lo, length, splits, world, 
     api = ("FoldWorkspace.append + " + (
         "PeerExchange.read_merge (far read + merge in one cooperative kernel)" if peer is not None and
         sharded is None else "ShardedFarMemory.step_merge (far read + peer exchange + merge in one "
-        "cooperative kernel)" if peer is not None else "ShardedFarMemory step/merge" if sharded is not None
+        "cooperative kernel)" if sharded is not None and fused else
+        f"ShardedFarMemory.step + merge ({args.exchange} exchange)" if sharded is not None
         else "FoldWorkspace.read_far + kernels.merge") + " (fold_b200 C-ABI), captured once per input buffer in a "
         "CUDA graph and replayed per step")
     return {"value": round(us_serial, 3), "unit": "us/draft-step",
