@@ -210,6 +210,13 @@ __device__ __forceinline__ bool named_bar_or(bool pred, int id, int nthreads) {
   return out != 0;
 }
 
+// The largest of three floats (an operand that is NaN is ignored, as by fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // 2^x through the SFU (x = -inf gives 0).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

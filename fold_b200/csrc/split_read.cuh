@@ -286,6 +286,41 @@ __device__ __forceinline__ void rotate_query_vec(const FarParams& p, const Query
   }
 }
 
+// Element-wise far-query rotation for the layouts the vector path does not take (unaligned rows of
+// q or qf, or a rotary size that is not whole 8-element chunks); trow as for rotate_query_vec.
+template <class C>
+__device__ __forceinline__ void rotate_query_scalar(const FarParams& p, const float* trow, int RH, float sgn, int h,
+                                                    int split, int nrows, int G, __nv_bfloat16* Qs) {
+  for (int e = threadIdx.x; e < C::ROWS * C::HD; e += C::NTHREADS) {
+    const int rho = e / C::HD, d = e - (e / C::HD) * C::HD;
+    float y = 0.f;
+    if (rho < nrows) {
+      const int r = rho / G, hq = h * G + (rho - r * G);
+      const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
+      const float x = bf2f(qr[d]);
+      if (trow && d < 2 * RH) {
+        const bool lo = d < RH;
+        const int i = lo ? d : d - RH;
+        const float xp = bf2f(qr[lo ? d + RH : d - RH]);
+        const float c = trow[i], s = sgn * trow[RH + i];
+        y = lo ? x * c - xp * s : x * c + xp * s;
+      } else {
+        y = x;
+      }
+      if constexpr (C::FP8) {
+        const __half yh = __float2half_rn(y);
+        *reinterpret_cast<__half*>(Qs + rho * C::QSTRIDE + (d & ~15) + fp8_slot(d & 15)) = yh;
+      } else {
+        const __nv_bfloat16 yb = __float2bfloat16_rn(y);
+        if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
+        Qs[rho * C::QSTRIDE + d] = yb;
+      }
+    } else {
+      Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);  // zero bits: 0 in f16 as well
+    }
+  }
+}
+
 // Window read: first and one-past-last visible position of row r (at position hist + r) under the
 // FlashAttention window [p - left, p + right] (a negative side is unbounded), causal or not,
 // within the seq context entries. Both grow with r.
@@ -434,34 +469,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     if (p.vec_rot) {
       rotate_query_vec<C>(p, ql, trow, rh8, RH, sgn, h, split, nrows, G, Qs);
     } else {
-      for (int e = tid; e < ROWS * HD; e += NTH) {
-        const int rho = e / HD, d = e - (e / HD) * HD;
-        float y = 0.f;
-        if (rho < nrows) {
-          const int r = rho / G, hq = h * G + (rho - r * G);
-          const __nv_bfloat16* qr = p.q + r * p.q_st + hq * p.q_sh;
-          const float x = bf2f(qr[d]);
-          if (trow && d < 2 * RH) {
-            const bool lo = d < RH;
-            const int i = lo ? d : d - RH;
-            const float xp = bf2f(qr[lo ? d + RH : d - RH]);
-            const float c = trow[i], s = sgn * trow[RH + i];
-            y = lo ? x * c - xp * s : x * c + xp * s;
-          } else {
-            y = x;
-          }
-          if constexpr (C::FP8) {
-            const __half yh = __float2half_rn(y);
-            *reinterpret_cast<__half*>(Qs + rho * C::QSTRIDE + (d & ~15) + fp8_slot(d & 15)) = yh;
-          } else {
-            const __nv_bfloat16 yb = __float2bfloat16_rn(y);
-            if (p.qf && split == 0) p.qf[r * p.qf_st + hq * p.qf_sh + d] = yb;
-            Qs[rho * C::QSTRIDE + d] = yb;
-          }
-        } else {
-          Qs[rho * C::QSTRIDE + d] = __float2bfloat16_rn(0.f);  // zero bits: 0 in f16 as well
-        }
-      }
+      rotate_query_scalar<C>(p, trow, RH, sgn, h, split, nrows, G, Qs);
     }
   }
   __syncthreads();  // barrier inits and the query tile are visible to every warp
@@ -554,10 +562,8 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     else return kRaise;
   };
   auto neg_max = [&](int j, int c) -> float { return MQ(j, c) == -INFINITY ? 0.f : -MQ(j, c); };
-  // P of QK n-tile j from its relative logits moved by sh[c], into P^T and the row sums.
-  auto store_p = [&](int j, const float (&sh)[2], float (&xs)[QNT][4], float (&lsum)[QNT][2], uint32_t pt) {
-    const float p0 = fast_exp2(xs[j][0] + sh[0]), p1 = fast_exp2(xs[j][1] + sh[1]);
-    const float p2 = fast_exp2(xs[j][2] + sh[0]), p3 = fast_exp2(xs[j][3] + sh[1]);
+  // P of QK n-tile j (keys g4 and g4 + 8, rows t4 * 2 and t4 * 2 + 1) into P^T and the row sums.
+  auto write_p = [&](int j, float p0, float p1, float p2, float p3, float (&lsum)[QNT][2], uint32_t pt) {
     const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
     lsum[j][0] = p0 + p2;
     lsum[j][1] = p1 + p3;
@@ -568,6 +574,11 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (ka * C::PSTRIDE + r0) * 2), "r"(pa));
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(pt + (kb * C::PSTRIDE + r0) * 2), "r"(pb));
     }
+  };
+  // P from the relative logits moved by sh[c] (after a raise of the row maxima).
+  auto store_p = [&](int j, const float (&sh)[2], float (&xs)[QNT][4], float (&lsum)[QNT][2], uint32_t pt) {
+    write_p(j, fast_exp2(xs[j][0] + sh[0]), fast_exp2(xs[j][1] + sh[1]), fast_exp2(xs[j][2] + sh[0]),
+            fast_exp2(xs[j][3] + sh[1]), lsum, pt);
   };
 
   bool timed_out = false;
@@ -629,16 +640,20 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       }
       // ---- scale, mask, and exponentiate relative to the current row maximum
       if (!WIN && tpos + TK <= open_end) {
+        // every key of the tile is visible to every row: one comparison of the thread's largest
+        // relative logit against kRaise decides
+        float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < QNT; ++j) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const float b = neg_max(j, c), t = THR(j, c);
+            const float b = neg_max(j, c);
             x[j][c] = fmaf(x[j][c], scale_log2, b);
             x[j][c + 2] = fmaf(x[j][c + 2], scale_log2, b);
-            exceed |= fmaxf(x[j][c], x[j][c + 2]) > t;
+            mx = fmax3(mx, x[j][c], x[j][c + 2]);
           }
         }
+        exceed = mx > kRaise;
       } else {
 #pragma unroll
         for (int j = 0; j < QNT; ++j) {
@@ -657,9 +672,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       if (it == 0) {
         exceed = true;  // the first tile always sets the row maxima: skip the provisional P
       } else {
-        const float zero[2] = {0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < QNT; ++j) store_p(j, zero, x, ls, pt);
+        for (int j = 0; j < QNT; ++j)
+          write_p(j, fast_exp2(x[j][0]), fast_exp2(x[j][1]), fast_exp2(x[j][2]), fast_exp2(x[j][3]), ls, pt);
       }
     }
 
