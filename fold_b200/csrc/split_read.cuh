@@ -536,11 +536,14 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     for (int b = 0; b < NT; ++b) oacc[a][b][0] = oacc[a][b][1] = oacc[a][b][2] = oacc[a][b][3] = 0.f;
   // Row maxima (log2 domain) of all rows this thread touches in PV; with NG > 1 the QK rows are a
   // subset kept separately (same values, computed from the same shared data).
+  // The far read starts them at 0 and its first tile always sets them (below), so they stay
+  // finite; the window read starts them at -inf (no maximum yet).
+  constexpr float kNoMax = WIN ? -INFINITY : 0.f;
   float mrow[NT][2], mq_own[NG == 1 ? 1 : QNT][2], lq[QNT][2];
 #pragma unroll
-  for (int b = 0; b < NT; ++b) mrow[b][0] = mrow[b][1] = -INFINITY;
+  for (int b = 0; b < NT; ++b) mrow[b][0] = mrow[b][1] = kNoMax;
 #pragma unroll
-  for (int j = 0; j < (NG == 1 ? 1 : QNT); ++j) mq_own[j][0] = mq_own[j][1] = -INFINITY;
+  for (int j = 0; j < (NG == 1 ? 1 : QNT); ++j) mq_own[j][0] = mq_own[j][1] = kNoMax;
 #pragma unroll
   for (int j = 0; j < QNT; ++j) lq[j][0] = lq[j][1] = 0.f;
   auto MQ = [&](int j, int c) -> float& {
@@ -552,8 +555,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   // kRaise, or -inf while the row has no maximum, so that its first finite logit sets one. The
   // far read needs no per-row threshold: its first tile, which always sets the maxima, holds a
   // visible key of every row that sees any key of the split (a row sees a prefix of the
-  // positions). Padding rows of the far read have zero queries, so logit 0 and P = 1 in open
-  // tiles: their columns of P^T and O are never written out.
+  // positions). A row without a key in that tile never sees one in the split; its maximum is kept
+  // at 0, so every far-read maximum is finite and the bias is -m itself. Padding rows of the far
+  // read have zero queries, so logit 0 and P = 1 in open tiles: their columns of P^T and O are
+  // never written out.
   float thr[WIN ? QNT : 1][2];
 #pragma unroll
   for (int j = 0; j < (WIN ? QNT : 1); ++j) thr[j][0] = thr[j][1] = -INFINITY;
@@ -561,7 +566,10 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     if constexpr (WIN) return thr[j][c];
     else return kRaise;
   };
-  auto neg_max = [&](int j, int c) -> float { return MQ(j, c) == -INFINITY ? 0.f : -MQ(j, c); };
+  auto neg_max = [&](int j, int c) -> float {
+    if constexpr (WIN) return MQ(j, c) == -INFINITY ? 0.f : -MQ(j, c);
+    else return -MQ(j, c);
+  };
   // P of QK n-tile j (keys g4 and g4 + 8, rows t4 * 2 and t4 * 2 + 1) into P^T and the row sums.
   auto write_p = [&](int j, float p0, float p1, float p2, float p3, float (&lsum)[QNT][2], uint32_t pt) {
     const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
@@ -690,7 +698,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         break;
       }
       // ---- raise the row maximum where a logit passed it by more than 2^kRaise (the shared
-      // row maxima are of the logits relative to the old maximum, the same in every warp)
+      // row maxima are of the logits relative to the old maximum, the same in every warp); the far
+      // read's first tile sets every maximum (its accumulators are still zero: factor 1)
+      const bool first = !WIN && it == 0;
 #pragma unroll
       for (int j = 0; j < QNT; ++j) {
 #pragma unroll
@@ -715,8 +725,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
           const float mo = mrow[nt][c];
           const float meo = mo == -INFINITY ? 0.f : mo;
           tm += meo;
-          const float mn = tm > mo + kRaise ? tm : mo;
-          const float f = mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
+          float mn = tm > mo + kRaise || first ? tm : mo;
+          if (!WIN && mn == -INFINITY) mn = 0.f;  // far read: no key of the split for this row
+          const float f = mn == -INFINITY || first ? 1.f : fast_exp2(mo - mn);
           mrow[nt][c] = mn;
           sh[c] = meo - (mn == -INFINITY ? 0.f : mn);
 #pragma unroll
@@ -744,8 +755,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
             const float mo = mq_own[j][c];
             const float meo = mo == -INFINITY ? 0.f : mo;
             tm += meo;
-            const float mn = tm > mo + kRaise ? tm : mo;
-            lq[j][c] *= mn == -INFINITY ? 1.f : fast_exp2(mo - mn);
+            float mn = tm > mo + kRaise || first ? tm : mo;
+            if (!WIN && mn == -INFINITY) mn = 0.f;
+            lq[j][c] *= mn == -INFINITY || first ? 1.f : fast_exp2(mo - mn);
             mq_own[j][c] = mn;
             sh[c] = meo - (mn == -INFINITY ? 0.f : mn);
             if constexpr (WIN) thr[j][c] = mn == -INFINITY ? -INFINITY : kRaise;
