@@ -49,8 +49,12 @@ __global__ void __launch_bounds__(kMergeWarps * 32) exchange_merge_kernel(const 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const MergeParams& m = p.m;
   // the epoch load is in flight while the first combine loads the partials; combine_slice's
-  // barrier publishes s_epoch
+  // barrier publishes s_epoch. The counter is written only by the previous exchange launch, which
+  // completed before this one's producer (the far read) started.
   if (threadIdx.x == 0) s_epoch = ld_relaxed_gpu(p.ex.ctr) + 1;
+  // Launched behind the far read: its partials (and every write of the kernels before it, which
+  // had completed when the far read released its dependents) are visible from here on.
+  wait_for_producer();
   const bool active = lane * 4 < min(p.hd, kSlice);
   uint32_t epoch = 0;
 
@@ -226,10 +230,15 @@ int fold_exchange_merge(void* exchange, const float* o_part, const float* lse_pa
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid), cfg.blockDim = dim3(kMergeWarps * 32), cfg.dynamicSmemBytes = 0;
   cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
+  // Cooperative, and behind the far read (programmatic stream serialisation): the blocks are
+  // scheduled as the far read's CTAs finish instead of after the whole grid has retired, and wait
+  // for it in wait_for_producer.
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
-  cfg.attrs = attr, cfg.numAttrs = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr, cfg.numAttrs = 2;
   st = check_cuda(cudaLaunchKernelEx(&cfg, exchange_merge_kernel, p), "exchange merge: launch");
   if (st) return st;
   return check_launch("exchange_merge_kernel");

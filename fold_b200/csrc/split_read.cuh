@@ -182,6 +182,7 @@ struct QueryLoad {
   static constexpr int ITEMS = C::ROWS * PAIRS;
   static constexpr int MAXI = (ITEMS + C::NTHREADS - 1) / C::NTHREADS;
   uint4 a[MAXI], b[MAXI];
+  float4 c0[MAXI], c1[MAXI], s0[MAXI], s1[MAXI];  // the rows' cos and sin (load_table_vec)
 };
 
 // rh8 = rotated 8-element chunks per half (0: no rotation).
@@ -207,29 +208,35 @@ __device__ __forceinline__ void load_query_vec(const FarParams& p, int rh8, int 
   }
 }
 
-// Vectorised far-query rotation of the loaded rows with the table row `trow` (cos then sin; read
-// only when rh8 > 0), written to the query tile Qs (and to qf by split 0). Every thread issues its
-// table loads before any arithmetic, so this costs one memory latency.
+// Issues the loads of the cos/sin values of the table row `trow` (cos then sin; read only when
+// rh8 > 0) that this thread's rotation items take. Called before the producer wait: no kernel that
+// releases its dependents early writes the table.
 template <class C>
-__device__ __forceinline__ void rotate_query_vec(const FarParams& p, const QueryLoad<C>& ql, const float* trow,
-                                                 int rh8, int RH, float sgn, int h, int split, int nrows, int G,
-                                                 __nv_bfloat16* Qs) {
-  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS, MAXI = QueryLoad<C>::MAXI;
-  const int tid = threadIdx.x;
-  float4 c0[MAXI], c1[MAXI], s0[MAXI], s1[MAXI];
+__device__ __forceinline__ void load_table_vec(const float* trow, int rh8, int RH, int nrows, QueryLoad<C>& ql) {
+  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS;
 #pragma unroll
-  for (int k = 0; k < MAXI; ++k) {
-    const int e = tid + k * C::NTHREADS;
-    c0[k] = c1[k] = s0[k] = s1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < QueryLoad<C>::MAXI; ++k) {
+    const int e = threadIdx.x + k * C::NTHREADS;
+    ql.c0[k] = ql.c1[k] = ql.s0[k] = ql.s1[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (e < ITEMS) {
       const int rho = e / PAIRS, c = e - (e / PAIRS) * PAIRS;
       if (rho < nrows && c < rh8) {
         const float4* tc = reinterpret_cast<const float4*>(trow + 8 * c);
         const float4* ts = reinterpret_cast<const float4*>(trow + RH + 8 * c);
-        c0[k] = __ldg(tc), c1[k] = __ldg(tc + 1), s0[k] = __ldg(ts), s1[k] = __ldg(ts + 1);
+        ql.c0[k] = __ldg(tc), ql.c1[k] = __ldg(tc + 1), ql.s0[k] = __ldg(ts), ql.s1[k] = __ldg(ts + 1);
       }
     }
   }
+}
+
+// Vectorised far-query rotation of the loaded rows with the loaded table values (load_query_vec,
+// load_table_vec), written to the query tile Qs (and to qf by split 0).
+template <class C>
+__device__ __forceinline__ void rotate_query_vec(const FarParams& p, const QueryLoad<C>& ql, int rh8, int RH,
+                                                 float sgn, int h, int split, int nrows, int G, __nv_bfloat16* Qs) {
+  constexpr int PAIRS = QueryLoad<C>::PAIRS, ITEMS = QueryLoad<C>::ITEMS, MAXI = QueryLoad<C>::MAXI;
+  const int tid = threadIdx.x;
+  const float4 *c0 = ql.c0, *c1 = ql.c1, *s0 = ql.s0, *s1 = ql.s1;
 #pragma unroll
   for (int k = 0; k < MAXI; ++k) {
     const int e = tid + k * C::NTHREADS;
@@ -413,6 +420,23 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
                          ? max(min(range_begin + range_tiles, tiles) - t_begin, 0)
                          : static_cast<int>(static_cast<int64_t>(tiles) * (split + 1) / nsplits) - t_begin;
 
+  // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table
+  // row of |D - H|; the row's loads are issued here. The window read takes the query as it is.
+  const float* trow = nullptr;
+  float sgn = 1.f;
+  bool rope_range = false;  // |D - H| past the table: recorded once the outputs may be written
+  if constexpr (!WIN) {
+    const int delta = p.far_distance - hist;
+    int ad = delta < 0 ? -delta : delta;
+    sgn = delta < 0 ? -1.f : 1.f;
+    if (p.table && ad >= p.table_rows) {
+      rope_range = true;
+      ad = p.table_rows - 1;
+    }
+    trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
+    if (p.vec_rot) load_table_vec<C>(trow, rh8, RH, nrows, ql);
+  }
+
   // Everything above read only the query, the lengths and the rope table, which no kernel that
   // releases its dependents early writes; the side cache and every output wait for the producer.
   wait_for_producer();
@@ -451,26 +475,11 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     }
   }
 
-  // Far query (fold/kernels.py:31-46): rotate by (D - H) * inv_freq with cos/sin from the table.
-  // The window read takes the query as it is.
-  {
-    const float* trow = nullptr;
-    float sgn = 1.f;
-    if constexpr (!WIN) {
-      const int delta = p.far_distance - hist;
-      int ad = delta < 0 ? -delta : delta;
-      sgn = delta < 0 ? -1.f : 1.f;
-      if (p.table && ad >= p.table_rows) {
-        if (tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
-        ad = p.table_rows - 1;
-      }
-      trow = p.table ? p.table + static_cast<int64_t>(ad) * p.rot_dim : nullptr;
-    }
-    if (p.vec_rot) {
-      rotate_query_vec<C>(p, ql, trow, rh8, RH, sgn, h, split, nrows, G, Qs);
-    } else {
-      rotate_query_scalar<C>(p, trow, RH, sgn, h, split, nrows, G, Qs);
-    }
+  if (rope_range && tid == 0 && split == 0 && h == 0) set_error(p.err, FOLD_DEVERR_ROPE_RANGE);
+  if (p.vec_rot) {
+    rotate_query_vec<C>(p, ql, rh8, RH, sgn, h, split, nrows, G, Qs);
+  } else {
+    rotate_query_scalar<C>(p, trow, RH, sgn, h, split, nrows, G, Qs);
   }
   __syncthreads();  // barrier inits and the query tile are visible to every warp
   if constexpr (WIN) {
