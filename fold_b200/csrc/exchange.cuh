@@ -7,8 +7,9 @@
 //   done  uint32 [kMaxKvHeads]: far-read splits finished per KV head in the current launch (the
 //         fused read; its last block zeroes them)
 // A record holds one item (row t, query head h, 128-column slice) of one rank's combined partial
-// in 16-byte lines {x, epoch, y, epoch}: 64 lines of o (lane l owns lines 2l and 2l+1, i.e.
-// columns 4l..4l+3) and one line with the LSE. Every 8-byte half of a line pairs a value with
+// in 16-byte lines {x, epoch, y, epoch}: 64 lines of o (lane l owns lines l and 32 + l, i.e.
+// columns 4l, 4l+1 and 4l+2, 4l+3, so that each warp-wide store covers 512 contiguous bytes: whole
+// 128-byte requests over NVLink) and one line with the LSE. Every 8-byte half of a line pairs a value with
 // the epoch that wrote it, and aligned 8-byte stores and loads are single-copy atomic, so a reader
 // that sees the current epoch in both halves of every line it needs has the current data: no
 // fence and no separate flag (the low-latency line format that NCCL's LL protocol also uses).
@@ -89,8 +90,8 @@ __device__ __forceinline__ bool read_record(const char* rec, int lane, bool acti
     const uint4 c = ld_line(rec + 64 * 16);
     uint4 a = c, b = c;
     if (active) {
-      a = ld_line(rec + (2 * lane) * 16);
-      b = ld_line(rec + (2 * lane + 1) * 16);
+      a = ld_line(rec + lane * 16);
+      b = ld_line(rec + (32 + lane) * 16);
     }
     if (line_is(a, epoch) && line_is(b, epoch) && line_is(c, epoch)) {
       o[0] = __uint_as_float(a.x), o[1] = __uint_as_float(a.z);
@@ -123,8 +124,8 @@ __device__ __forceinline__ void exchange_item(const ExchangeView& ex, const Merg
     if (r == ex.rank) continue;
     char* rec = ex.recv[r] + mine;
     if (active) {
-      st_line(rec + (2 * lane) * 16, of[0], of[1], epoch);
-      st_line(rec + (2 * lane + 1) * 16, of[2], of[3], epoch);
+      st_line(rec + lane * 16, of[0], of[1], epoch);
+      st_line(rec + (32 + lane) * 16, of[2], of[3], epoch);
     }
     if (lane == 0) st_line(rec + 64 * 16, lse_far, lse_far, epoch);
   }
