@@ -605,13 +605,15 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   float scale_log2 = p.scale_log2, out_scale = 1.f;
   if constexpr (C::FP8) scale_log2 *= __ldg(p.k_scale + h), out_scale = __ldg(p.v_scale + h);
 
+  // Ring position of the current tile and of the previous one, the current stage's mbarrier
+  // phase and the tile's first position, advanced per tile (no division in the loop).
+  int st = 0, st_prev = NSTAGE - 1;
+  uint32_t phase = 0;
+  int64_t tpos = pos0 + static_cast<int64_t>(t_begin) * TK;
   for (int it = 0; it < ntiles; ++it) {
-    const int st = it % NSTAGE;
-    const bool ok = mbar_wait(&full[st], (it / NSTAGE) & 1);
-    const int tile = t_begin + it;  // this tile's index in the cache
+    const bool ok = mbar_wait(&full[st], phase);
     const uint32_t kv_base = smem_u32(smem + st * C::STAGE_BYTES);
     const uint32_t pt = p_base + (it & 1) * (TK * C::PSTRIDE * 2);
-    const int64_t tpos = pos0 + static_cast<int64_t>(tile) * TK;  // first position of the tile
     const int64_t key0 = tpos + mt * 16 + g4;
 
     float x[QNT][4];
@@ -698,8 +700,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
     // One barrier per tile: P^T of every warp is written, every warp is done with the previous
     // tile (so its stage may be refilled), and the CTA learns whether any row maximum must move.
     const bool attention = named_bar_or(exceed || !ok, 1, NTH);
-    if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles)
-      issue((it - 1) % NSTAGE, t_begin + it - 1 + NSTAGE);
+    if ((WIN || tid == 0) && it >= 1 && it - 1 + NSTAGE < ntiles) issue(st_prev, t_begin + it - 1 + NSTAGE);
     if (attention) {
       if (named_bar_or(!ok, 2, NTH)) {
         timed_out = true;
@@ -818,6 +819,9 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       }
     }
     consumed = it + 1;
+    st_prev = st;
+    if (++st == NSTAGE) st = 0, phase ^= 1u;
+    tpos += TK;
   }
 
   // -------------------------------------------------------------- epilogue
