@@ -217,6 +217,23 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// a0 = a0 * s + b0 and a1 = a1 * s + b1 as one packed two-lane FP32 instruction.
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float s, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, m, b;\n\t"
+      "mov.b64 x, {%0, %1};\n\tmov.b64 m, {%2, %2};\n\tmov.b64 b, {%3, %4};\n\t"
+      "fma.rn.f32x2 x, x, m, b;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(s), "f"(b0), "f"(b1));
+}
+// (d0, d1) = (a0 + b0, a1 + b1) as one packed two-lane FP32 instruction.
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // 2^x through the SFU (x = -inf gives 0).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -582,8 +582,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
   // P of QK n-tile j (keys g4 and g4 + 8, rows t4 * 2 and t4 * 2 + 1) into P^T and the row sums.
   auto write_p = [&](int j, float p0, float p1, float p2, float p3, float (&lsum)[QNT][2], uint32_t pt) {
     const uint32_t pa = pack_f16_sat(p0, p1), pb = pack_f16_sat(p2, p3);
-    lsum[j][0] = p0 + p2;
-    lsum[j][1] = p1 + p3;
+    fadd2(lsum[j][0], lsum[j][1], p0, p1, p2, p3);
     if (nt_lo + j < NT) {
       const int r0 = (nt_lo + j) * 8 + t4 * 2;
       // P^T row of keys g4 and g4 + 8 (fp8: their fragment slots, the order V^T gives keys in)
@@ -664,13 +663,12 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
         float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < QNT; ++j) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const float b = neg_max(j, c);
-            x[j][c] = fmaf(x[j][c], scale_log2, b);
-            x[j][c + 2] = fmaf(x[j][c + 2], scale_log2, b);
-            mx = fmax3(mx, x[j][c], x[j][c + 2]);
-          }
+          // keys g4 and g4 + 8 of the row pair (t4 * 2, t4 * 2 + 1): packed FMAs with the rows' biases
+          const float b0 = neg_max(j, 0), b1 = neg_max(j, 1);
+          ffma2(x[j][0], x[j][1], scale_log2, b0, b1);
+          ffma2(x[j][2], x[j][3], scale_log2, b0, b1);
+          mx = fmax3(mx, x[j][0], x[j][1]);
+          mx = fmax3(mx, x[j][2], x[j][3]);
         }
         exceed = mx > kRaise;
       } else {
@@ -778,7 +776,7 @@ __device__ __forceinline__ void split_read(const CUtensorMap* map, const CUtenso
       named_bar_sync(2, NTH);
     }
 #pragma unroll
-    for (int j = 0; j < QNT; ++j) lq[j][0] += ls[j][0], lq[j][1] += ls[j][1];
+    for (int j = 0; j < QNT; ++j) fadd2(lq[j][0], lq[j][1], lq[j][0], lq[j][1], ls[j][0], ls[j][1]);
 
     // ---- O^T += V^T . P^T over this warp's hd group and key group
 #pragma unroll
